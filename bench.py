@@ -1,0 +1,414 @@
+"""Benchmark of MORPH's optimizer-step hot path on B200 (one JSON line).
+
+Workload: the dense 5B-shaped AdamW step — 42 layers of
+{3 x [3072, 6144], 4 x [3072, 3072], 4 x [3072]} plus a [65536, 3072] tied
+embedding = 4,165,459,968 FP32 masters with FP32 m and v, BF16 gradients
+N(0, 1e-4), global-norm clip at 1.0 (torch clip_grad_norm_ rule), AdamW
+lr 3e-4, betas (.9, .95), eps 1e-8, weight decay .1, BF16 compute copy written
+by the update. Parameters are flat-sharded ZeRO-1 style over the ranks; each
+step all-reduces the 16-byte {sum of squares, nonfinite} record and, with N > 1,
+all-gathers the updated BF16 shards.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl morph|reference]
+
+``value`` is params/s of the whole job (device-timed with CUDA events, max over
+ranks, inputs resident in HBM; 116.6 GB of algorithmic traffic per step is far
+larger than the 126 MB L2, so no flush is needed). ``e2e`` is the same metric
+through the public ``morph_b200.AdamW.step()`` with the BF16 gradients copied
+from pinned host memory every step and the step record (norm, skip) read back.
+``--impl reference`` times the reference's CPU step (torch.optim.AdamW with
+foreach=False after clip_grad_norm_, morph/training/runner.py:100-101) on the
+host cores over a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "AdamW step params/s & HBM GB/s (% of ~8 TB/s) at 4.2B params, 1/2/4/8 B200"
+LR, BETAS, EPS, WD, MAX_NORM = 3e-4, (0.9, 0.95), 1e-8, 0.1, 1.0
+APPLY_BYTES = 28   # kernel 1: g 2 R + w,m,v 12 R + w,m,v 12 W + BF16 copy 2 W
+STATS_BYTES = 2    # kernel 2: g 2 R
+FALLBACK_HBM_GBS = 6650.0
+
+
+def config2_shapes():
+    shapes = []
+    for layer in range(42):
+        shapes += [(f"blocks.{layer}.ffn.{n}", (3072, 6144)) for n in ("gate", "up", "down")]
+        shapes += [(f"blocks.{layer}.ssm.{n}", (3072, 3072)) for n in ("in", "x", "z", "out")]
+        shapes += [(f"blocks.{layer}.vec.{n}", (3072,)) for n in ("norm", "bias", "dt_bias", "skip")]
+    shapes.append(("embedding.weight", (65536, 3072)))
+    return shapes
+
+
+def numel(shape):
+    n = 1
+    for s in shape:
+        n *= s
+    return n
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        # nvidia-smi addresses GPUs by physical index or UUID; CUDA_VISIBLE_DEVICES
+        # may renumber, so use the UUID of the torch device.
+        try:
+            self.index = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+        except Exception:
+            self.index = str(device_index)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=10)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- CPU side --
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def reference_cpu_step_time(layers=1, steps=3, warmup=1, seed=0):
+    """Time the reference's CPU step on a bounded sample of config 2: ``layers``
+    layers (94,384,128 params each) through torch.nn.utils.clip_grad_norm_
+    (max_norm 1.0) and torch.optim.AdamW(foreach=False) — the calls at
+    morph/training/runner.py:100-101 with the optimizer of
+    streamtrain/optimizer.py:40 — on every host thread. Returns
+    (params per step, seconds per step list, threads)."""
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(seed)
+    shapes = [s for _, s in config2_shapes()[: 11 * layers]]
+    params = [torch.nn.Parameter(torch.randn(s, generator=g) * 0.02) for s in shapes]
+    grads = [(torch.randn(s, generator=g) * 1e-4).to(torch.bfloat16) for s in shapes]
+    opt = torch.optim.AdamW(params, lr=LR, betas=BETAS, eps=EPS, weight_decay=WD, foreach=False)
+    times = []
+    for i in range(warmup + steps):
+        for p, gr in zip(params, grads):
+            p.grad = gr.float()
+        t0 = time.perf_counter()
+        torch.nn.utils.clip_grad_norm_(params, MAX_NORM)
+        opt.step()
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+    return sum(numel(s) for s in shapes), times, threads
+
+
+def run_reference(args, rank):
+    """``--impl reference``: the reference's CPU step on host cores, rank 0 only."""
+    if rank != 0:
+        return
+    n, times, threads = reference_cpu_step_time(layers=1, steps=args.steps, warmup=args.warmup)
+    sec = sum(times) / len(times)
+    value = n / sec
+    sample = (f"1 of 42 layers of config 2 ({n:,} params: 3x[3072,6144], 4x[3072,3072], 4x[3072]) per step; "
+              "clip_grad_norm_(1.0) + torch.optim.AdamW(foreach=False), FP32 grads from BF16")
+    line = {"metric": METRIC, "value": value, "unit": "params/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "config2: dense 5B-shaped AdamW step, CPU sample", "params_per_step": n},
+            "cpu_baseline": {"value": value, "unit": "params/s", "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "params/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU side --
+
+def shard_bounds(total, world, rank, align=16):
+    per = -(-total // world)
+    per = -(-per // align) * align
+    lo = min(total, rank * per)
+    hi = min(total, lo + per)
+    return lo, hi
+
+
+def run_morph(args, rank, world, local_rank):
+    import torch.distributed as dist
+    from morph_b200 import AdamW, _lib
+    from morph_b200.optim import StepEngine
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    shapes = config2_shapes()
+    sizes = [numel(s) for _, s in shapes]
+    total = sum(sizes)
+    lo, hi = shard_bounds(total, world, rank)
+    n_local = hi - lo
+    per = shard_bounds(total, world, 0)[1]  # padded shard length; every rank allocates it
+
+    # Flat shard buffers: FP32 w, m, v; BF16 gradient shard; the full BF16 weights
+    # (this rank's slice of it is where the update writes its BF16 copy).
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    w = torch.empty(per, dtype=torch.float32, device=device)
+    chunk = 1 << 28
+    for s in range(0, per, chunk):
+        e = min(per, s + chunk)
+        w[s:e].normal_(0.0, 0.02, generator=gen)
+    m = torch.zeros_like(w)
+    v = torch.zeros_like(w)
+    g = torch.empty(per, dtype=torch.bfloat16, device=device)
+    for s in range(0, per, chunk):
+        e = min(per, s + chunk)
+        g[s:e] = torch.empty(e - s, device=device).normal_(0.0, 1e-4, generator=gen).to(torch.bfloat16)
+    full16 = torch.zeros(per * world, dtype=torch.bfloat16, device=device)
+    out = full16[rank * per:(rank + 1) * per]
+
+    # Segments: pieces of the model's tensors inside this rank's shard.
+    pieces = []
+    off = 0
+    for (name, shape), n in zip(shapes, sizes):
+        a, b = max(off, lo), min(off + n, hi)
+        if a < b:
+            pieces.append((a - lo, b - a))
+        off += n
+    eng = StepEngine(device)
+    views = [(w[o:o + n], m[o:o + n], v[o:o + n], g[o:o + n], out[o:o + n]) for o, n in pieces]
+    for vw in views:
+        eng.slot(vw[0], 0)
+    entries = [(vw[0], vw[1], vw[2], vw[3], vw[4], 0) for vw in views]
+    groups = [(LR, BETAS[0], BETAS[1], EPS, WD, "torch")]
+    plan = eng.prepare(entries, groups, _lib.MB_BF16, _lib.MB_BF16)
+    fin = eng.finalize_opts(_lib.MB_FIN_CLIP_TORCH | _lib.MB_FIN_GATE, MAX_NORM)
+    lib = eng.lib
+    import ctypes
+    pp, pf = ctypes.byref(plan), ctypes.byref(fin)
+    record = eng.state_buf[:16].view(torch.float64)
+
+    def one_step(evs=None):
+        s = _lib.stream_handle()
+        if evs is not None:
+            evs[0].record()
+        if world == 1:
+            _lib.check(lib.mb_grad_stats(pp, pf, s))
+        else:
+            _lib.check(lib.mb_grad_stats(pp, None, s))
+            dist.all_reduce(record)
+            _lib.check(lib.mb_step_finalize(pp, pf, s))
+        if evs is not None:
+            evs[1].record()
+        _lib.check(lib.mb_adamw_apply(pp, s))
+        eng.max_clock += 1
+        if evs is not None:
+            evs[2].record()
+        if world > 1:
+            dist.all_gather_into_tensor(full16, out)
+        if evs is not None:
+            evs[3].record()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        one_step()
+    barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        barrier()
+        start.record()
+        for i in range(args.steps):
+            one_step(evs[i])
+        stop.record()
+        barrier()
+    total_ms = start.elapsed_time(stop)
+    stats_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
+    apply_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+    gather_ms = sum(e[2].elapsed_time(e[3]) for e in evs) / args.steps
+    st = eng.read_state()
+    if st.status or st.skip:
+        raise RuntimeError(f"bench step refused: status {st.status} skip {st.skip}")
+    t = torch.tensor([total_ms, stats_ms, apply_ms, gather_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, stats_ms, apply_ms, gather_ms = t.tolist()
+    ms_per_step = total_ms / args.steps
+    value = total / (ms_per_step / 1e3)
+    clocks = clk.summary()
+    del views, entries, plan
+
+    # e2e through the public API: AdamW.step() on the model's tensors, gradients
+    # copied from pinned host memory each step, the step record read back.
+    e2e = None
+    if not args.no_e2e and world == 1:
+        e2e = run_e2e(args, device, shapes, sizes, w[:total], m[:total], v[:total], g[:total], out[:total])
+
+    hbm, peak_kind = measured_peaks()
+    achieved = APPLY_BYTES * n_local / (apply_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2: dense 5B-shaped AdamW step (4,165,459,968 params, BF16 grads, "
+                               "clip 1.0, BF16 compute copy)",
+                   "params": total, "grad_dtype": "bf16", "parallelism": f"zero1-dp{world}",
+                   "l2": "inputs larger than L2 (116.6 GB of traffic per step vs 126 MB L2); no flush"},
+        "hbm_gbs": (APPLY_BYTES + STATS_BYTES) * total / (ms_per_step / 1e3) / 1e9,
+        "kernels_ms": {"grad_stats": stats_ms, "adamw_apply": apply_ms, "all_gather": gather_ms},
+        "roofline": {"bound": "hbm", "kernel": "mb_adamw_apply", "achieved": achieved, "peak": hbm,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
+                     "algorithmic_bytes_per_launch": APPLY_BYTES * n_local, "traffic": None},
+        "gpu_launches": 2 * args.steps if world == 1 else 3 * args.steps,
+        "clocks": clocks,
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        n, times, threads = reference_cpu_step_time(layers=1, steps=3, warmup=1)
+        line["cpu_baseline"] = {"value": n / (sum(times) / len(times)), "unit": "params/s", "cores": threads,
+                                "kind": "reference",
+                                "sample": f"1 of 42 layers ({n:,} params), clip_grad_norm_ + "
+                                          "torch.optim.AdamW(foreach=False), 3 timed steps"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, device, shapes, sizes, w, m, v, g, out):
+    from morph_b200 import AdamW
+    params, off = [], 0
+    for (name, shape), n in zip(shapes, sizes):
+        p = torch.nn.Parameter(w[off:off + n].view(shape))
+        p.grad_dtype = None  # BF16 gradients on FP32 masters
+        p.grad = g[off:off + n].view(shape)
+        params.append((p, off, n))
+        off += n
+    opt = AdamW([p for p, _, _ in params], lr=LR, betas=BETAS, eps=EPS, weight_decay=WD, foreach=False,
+                max_norm=MAX_NORM, gate=True, sync=False, low_precision=torch.bfloat16)
+    for p, o, n in params:
+        st = opt.state[p]
+        st["exp_avg"] = m[o:o + n].view(p.shape)
+        st["exp_avg_sq"] = v[o:o + n].view(p.shape)
+        opt.low_precision_copies[p] = out[o:o + n].view(p.shape)
+    host = torch.empty(g.numel(), dtype=torch.bfloat16, pin_memory=True)
+    host.copy_(g)
+    rec_host = torch.empty(96, dtype=torch.uint8, pin_memory=True)
+    eng_state = None
+    steps = max(1, min(args.steps, 5))
+
+    def step():
+        nonlocal eng_state
+        g.copy_(host, non_blocking=True)
+        opt.step()
+        if eng_state is None:
+            eng_state = opt._engine.state_buf
+        rec_host.copy_(eng_state, non_blocking=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / steps
+    total = g.numel()
+    return {"value": total / (ms / 1e3), "unit": "params/s", "ms_per_step": ms, "steps": steps,
+            "h2d_bytes_per_step": total * 2, "d2h_bytes_per_step": 96,
+            "path": "morph_b200.AdamW.step(), 463 tensors, grads H2D from pinned host"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["morph", "reference"], default="morph")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "morph":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_morph(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,207 @@
+/*
+ * morph_b200 — C ABI of the B200 optimizer-step kernels.
+ *
+ * Every entry point takes raw device pointers, element counts, dtype codes and
+ * a CUDA stream, returns an int status (MB_OK = 0) and throws nothing. No entry
+ * point allocates parameter memory or synchronises the host with the device;
+ * callers own every buffer (state, workspace, tables) and size the workspace
+ * with mb_workspace_bytes().
+ *
+ * Reference interfaces replaced (paths inside the everett6/MORPH project):
+ *   mb_adamw_step / mb_grad_stats / mb_step_finalize / mb_adamw_apply
+ *       torch.optim.AdamW(..., betas=(.9,.95), foreach=False).step() built at
+ *       streamtrain/optimizer.py:40 and stepped at streamtrain/optimizer.py:62 and
+ *       morph/training/runner.py:101; the finiteness gate at
+ *       streamtrain/optimizer.py:50-51; clip_grad_norm_ at morph/training/runner.py:100;
+ *       the FP64 norm pass at streamtrain/disk.py:466-468 and
+ *       streamtrain/sparse_disk.py:136; DynamicLossScale.overflow/success at
+ *       streamtrain/precision.py:9-14 as driven by streamtrain/disk.py:482-497.
+ *   mb_adamw_update
+ *       DiskState.update(name, gradient, step, lr, clip) at streamtrain/disk.py:203-223
+ *       (and CachedDiskState.update at streamtrain/state_cache.py:103-140), with the
+ *       gradient unscale g.float()/loss_scale of streamtrain/sparse_disk.py:107.
+ *   mb_sparse_rows_update
+ *       the conditional AdamW of streamtrain/sparse_disk.py:122-138 applied to the
+ *       touched rows of one table (DiskState.update on the gathered rows).
+ *   mb_cast_f32
+ *       the FP32 -> BF16/FP16 compute copy (streamtrain/disk.py:320-326,351) and the
+ *       FP16 export with its range check (streamtrain/export.py:32-34).
+ */
+#ifndef MORPH_B200_H
+#define MORPH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MB_API __attribute__((visibility("default")))
+
+/* Same object as cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st* mb_stream_t;
+
+/* ------------------------------------------------------------- status -- */
+enum {
+  MB_OK = 0,
+  MB_ERR_ARG = 1,                /* null pointer, negative size, unknown dtype/flag  */
+  MB_ERR_ALIGN = 2,              /* pointer alignment below the entry's contract     */
+  MB_ERR_CUDA = 3,               /* a CUDA runtime call or launch failed             */
+  MB_ERR_OVERFLOW_MIN_SCALE = 4, /* FP16 overflow while the loss scale is already 1  */
+  MB_ERR_NONFINITE = 5,          /* nonfinite gradient with the finiteness gate on   */
+  MB_ERR_TIMEOUT = 6,            /* a bounded wait expired                           */
+  MB_ERR_INDEX = 7,              /* a row index outside the table                    */
+  MB_ERR_UNREPRESENTABLE = 8     /* FP16 export of a nonfinite value or |w| > 65504  */
+};
+
+/* ------------------------------------------------------------- dtypes -- */
+enum { MB_F32 = 0, MB_F16 = 1, MB_BF16 = 2, MB_NONE = 3 };
+
+/* ------------------------------------------------- multi-tensor AdamW -- */
+
+/* One contiguous run of elements of one parameter tensor. w, m, v are FP32;
+ * g has the plan's grad dtype; out (optional) receives the updated w in the
+ * plan's out dtype (round to nearest even). Vector loads are used when w, m,
+ * v (and an FP32 g) are 16-byte aligned and a 16-bit g / out is 8-byte
+ * aligned; other segments take the scalar path. */
+typedef struct mb_segment {
+  float* w;
+  float* m;
+  float* v;
+  const void* g;
+  void* out;
+  int64_t numel;
+  int64_t tile_begin; /* set by mb_segments_plan */
+  int32_t clock;      /* index into the plan's clock array; unique per segment */
+  int32_t group;      /* index into the plan's group array */
+} mb_segment;
+
+/* Hyperparameters of one parameter group. Float fields are the float32
+ * roundings of the double expressions named, computed by the caller exactly as
+ * the reference's Python does. */
+typedef struct mb_group {
+  double lr;    /* step size numerator: scalar = (float)(-(lr / bc1[t]))  */
+  float cwd;    /* (float)(1 - lr * weight_decay)                         */
+  float omb1;   /* (float)(1 - beta1): lerp weight of the first moment    */
+  float beta2;  /* (float)beta2                                           */
+  float omb2;   /* (float)(1 - beta2): addcmul value of the second moment */
+  float eps;    /* (float)eps                                             */
+  int32_t table;/* row of the bias-correction table                       */
+} mb_group;
+
+/* Device-resident step control, one per optimizer. sumsq and nonfinite come
+ * first: that 16-byte record is what ranks all-reduce (SUM, FP64). */
+typedef struct mb_step_state {
+  double sumsq;           /* sum of squared unscaled gradients (FP64)           */
+  double nonfinite;       /* number of nonfinite gradient elements              */
+  double scale;           /* loss scale the next step's gradients carry         */
+  double step_scale;      /* loss scale the last finalized step divided by      */
+  int64_t good_steps;     /* DynamicLossScale.good_steps                        */
+  int64_t growth_interval;/* DynamicLossScale.growth_interval                   */
+  double max_scale;       /* growth cap (65536 in the reference)                */
+  double norm;            /* sqrt(sumsq) of the last finalized step             */
+  float clip_coef;        /* multiplier applied to unscaled gradients           */
+  int32_t skip;           /* 1 if the last finalized step skips its update      */
+  int32_t status;         /* MB_OK, MB_ERR_OVERFLOW_MIN_SCALE or MB_ERR_NONFINITE*/
+  int32_t steps_applied;  /* updates applied so far                             */
+  int32_t steps_skipped;  /* updates skipped so far                             */
+  int32_t reserved[3];
+} mb_step_state;
+
+/* Finalize flags. */
+enum {
+  MB_FIN_LOSS_SCALE = 1, /* divide grads by state.scale; on nonfinite back off, else success() */
+  MB_FIN_GATE = 2,       /* without loss scaling: nonfinite -> skip, status MB_ERR_NONFINITE   */
+  MB_FIN_CLIP_TORCH = 4, /* coef = min(1, fl32(1/(fl32(norm) + 1e-6f)) * max_norm)           */
+  MB_FIN_CLIP_DISK = 8   /* coef = (float)min(1, max_norm / (norm + 1e-6)) in double          */
+};
+
+typedef struct mb_finalize_opts {
+  int32_t flags;
+  int32_t reserved;
+  double max_norm;  /* clip threshold (> 0 when a clip flag is set) */
+  double backoff;   /* loss-scale factor on overflow (0.5 in the reference) */
+  double growth;    /* loss-scale factor after growth_interval good steps (2.0) */
+} mb_finalize_opts;
+
+/* Everything one fused multi-tensor AdamW launch needs. All pointers are
+ * device pointers except that the struct itself is read on the host. */
+typedef struct mb_adamw_plan {
+  const mb_segment* segs;  /* n_segs entries, tile_begin planned                   */
+  const mb_group* groups;  /* n_groups entries                                     */
+  const double* bc;        /* [tables][2][bc_len]: 1 - beta1**t, sqrt(1 - beta2**t)*/
+  int32_t* clocks;         /* per-segment step counters (torch state['step'])      */
+  void* workspace;         /* mb_workspace_bytes(n_segs) bytes, 256-byte aligned   */
+  mb_step_state* state;
+  int64_t n_tiles;         /* from mb_segments_plan                                */
+  int64_t bc_len;          /* clocks beyond bc_len-1 read the last entry           */
+  int32_t n_segs;
+  int32_t n_groups;
+  int32_t grad_dtype;      /* MB_F32, MB_F16 or MB_BF16                            */
+  int32_t out_dtype;       /* MB_F16, MB_BF16 or MB_NONE                           */
+} mb_adamw_plan;
+
+MB_API int mb_version(void);
+MB_API const char* mb_status_string(int status);
+
+/* Host only: fills segs[i].tile_begin and returns the tile count. */
+MB_API int mb_segments_plan(mb_segment* segs_host, int32_t n_segs, int64_t* n_tiles);
+
+/* Bytes of device workspace a plan with n_segs segments needs. */
+MB_API size_t mb_workspace_bytes(int32_t n_segs);
+
+/* Host only: a fresh step state (scale, growth interval; everything else 0,
+ * clip_coef 1, max_scale 65536). Copy it to the device yourself. */
+MB_API int mb_step_state_init(mb_step_state* host_state, double scale, int64_t growth_interval);
+
+/* Kernel 2: FP64 sum of squares and nonfinite count of all plan gradients
+ * (unscaled by state.scale when fin has MB_FIN_LOSS_SCALE). Writes
+ * state.sumsq/nonfinite; with fin != NULL it also finalizes in the same launch. */
+MB_API int mb_grad_stats(const mb_adamw_plan* plan, const mb_finalize_opts* fin, mb_stream_t stream);
+
+/* One block: loss-scale transition, skip decision, clip coefficient, clock
+ * advance and per-segment step scalars, from state.sumsq/nonfinite. */
+MB_API int mb_step_finalize(const mb_adamw_plan* plan, const mb_finalize_opts* fin, mb_stream_t stream);
+
+/* Kernel 1: the fused AdamW update of every segment (early exit when
+ * state.skip), writing the optional low-precision copy. */
+MB_API int mb_adamw_apply(const mb_adamw_plan* plan, mb_stream_t stream);
+
+/* mb_grad_stats (fused finalize) followed by mb_adamw_apply. */
+MB_API int mb_adamw_step(const mb_adamw_plan* plan, const mb_finalize_opts* fin, mb_stream_t stream);
+
+/* --------------------------------------- single tensor, host scalars -- */
+
+/* Step scalars computed on the host (float32 roundings of the reference's
+ * double expressions). grad' = (g / scale) * coef before the update. */
+typedef struct mb_host_scalars {
+  float cwd, omb1, beta2, omb2, bc2s, eps, nss;
+  float scale; /* loss-scale divisor (1 for none) */
+  float coef;  /* clip multiplier (1 for none) */
+} mb_host_scalars;
+
+/* DiskState.update on one device-resident tensor (w, m, v FP32). */
+MB_API int mb_adamw_update(float* w, float* m, float* v, const void* g, int32_t grad_dtype,
+                           void* out, int32_t out_dtype, int64_t numel,
+                           const mb_host_scalars* s, mb_stream_t stream);
+
+/* Kernel 3: lazy row-sparse AdamW. Rows idx[0..k) of the [rows, cols] FP32
+ * planes w, m, v take one step with gradient row r = grads[r*cols ..]. Rows not
+ * listed are not read or written. An index outside [0, rows) is skipped and
+ * sets *err_flag (device int32, may be NULL) to 1. cols must be a multiple of 4. */
+MB_API int mb_sparse_rows_update(float* w, float* m, float* v, int64_t rows, int64_t cols,
+                                 const int64_t* idx, int64_t k, const void* grads,
+                                 int32_t grad_dtype, const mb_host_scalars* s,
+                                 int32_t* err_flag, mb_stream_t stream);
+
+/* FP32 -> F16/BF16 cast (round to nearest even). With check != 0 (F16 only)
+ * a nonfinite value or |x| > 65504 sets *err_flag to 1 (export.py:33). */
+MB_API int mb_cast_f32(const float* src, void* dst, int32_t dst_dtype, int64_t n, int32_t check,
+                       int32_t* err_flag, mb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MORPH_B200_H */

@@ -1,0 +1,16 @@
+"""morph_b200 — MORPH's optimizer-step hot path as hand-written sm_100a kernels.
+
+Public drop-ins (same names and behaviour as the reference's interfaces):
+  AdamW               torch.optim.AdamW as built at streamtrain/optimizer.py:40
+  DynamicLossScale    streamtrain/precision.py:6-17, state resident on the GPU
+  HybridMuonAdamW     streamtrain/optimizer.py:34-70 (Muon + AdamW)
+  DeviceDiskState     DiskState.update arithmetic (streamtrain/disk.py:203-223)
+                      on device-resident [w; m; v] planes, plus the row-sparse update
+
+All compute goes through the C-ABI library libmorph_b200.so (include/morph_b200.h);
+importing a class that needs it raises ImportError when the library is missing.
+"""
+from .precision import DynamicLossScale, fp8_eligible
+from .optim import AdamW
+
+__all__ = ["AdamW", "DynamicLossScale", "fp8_eligible"]

@@ -1,0 +1,526 @@
+// Kernels 1 and 2 of the optimizer step: the fused multi-tensor AdamW update
+// and the gradient statistics pass with its on-device finalize.
+//
+// Reference semantics (paths inside the MORPH project):
+//   update     torch/optim/adam.py _single_tensor_adam (torch 2.11.0), as built at
+//              streamtrain/optimizer.py:40 and stepped at optimizer.py:62 /
+//              morph/training/runner.py:101; DiskState.update streamtrain/disk.py:207-215.
+//   statistics streamtrain/disk.py:466-468 (FP64 squares), optimizer.py:50-51 (gate).
+//   finalize   streamtrain/precision.py:9-14 (overflow/success), disk.py:482-489
+//              (skip + backoff, clip), clip_grad.py:165-169 (torch clip coefficient).
+//
+// Layout: the plan's segments cover the parameters in a fixed order; each
+// segment starts on a fresh 2048-element tile. A CTA sweeps a tile in two
+// coalesced passes of 1024 elements (thread t owns elements 4t..4t+3 of each
+// pass), so every warp-wide access is one contiguous 512 B (FP32) or 256 B
+// (16-bit) run. The grid is persistent (CTAs resident on all SMs) and strides
+// over tiles.
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "mb_common.cuh"
+
+namespace mb {
+
+int persistent_blocks(const void* kernel, int threads, size_t smem) {
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess) return 0;
+  if (per_sm < 1) per_sm = 1;
+  return sms * per_sm;
+}
+
+int grid_for(const void* fn, int64_t n_tiles) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int blocks;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find({fn, dev});
+    if (it == cache.end()) it = cache.emplace(std::make_pair(fn, dev), persistent_blocks(fn, kThreads, 0)).first;
+    blocks = it->second;
+  }
+  int64_t b = blocks > 0 ? blocks : 148;
+  if (b > n_tiles) b = n_tiles;
+  return (int)(b < 1 ? 1 : b);
+}
+
+namespace {
+
+struct ApplyArgs {
+  const mb_segment* segs;
+  const mb_group* groups;
+  const float2* seg_scal;  // per-segment {nss, bc2s} from the finalize
+  const mb_step_state* state;
+  int64_t n_tiles;
+  int32_t n_segs;
+};
+
+__device__ __forceinline__ StepScalars group_scalars(const mb_group& g, float2 ss) {
+  StepScalars s;
+  s.small = fabsf(g.omb1) < 0.5f;
+  s.lw = s.small ? g.omb1 : __fsub_rn(g.omb1, 1.0f);
+  s.cwd = g.cwd;
+  s.b2 = g.beta2;
+  s.omb2 = g.omb2;
+  s.eps = g.eps;
+  s.nss = ss.x;
+  s.bc2s = ss.y;
+  return s;
+}
+
+// Update the 4 elements at e (vector path) of one segment.
+template <int GDT, int ODT>
+__device__ __forceinline__ void apply_quad(const mb_segment& seg, int64_t e, const StepScalars& s,
+                                           const GradPrep& prep) {
+  float g[4];
+  load4<GDT>(seg.g, e, g);
+  float4 w = ld4f(seg.w + e), m = ld4f(seg.m + e), v = ld4f(seg.v + e);
+  float ww[4] = {w.x, w.y, w.z, w.w}, mm[4] = {m.x, m.y, m.z, m.w}, vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) adam_elem(ww[j], mm[j], vv[j], prep(g[j]), s);
+  st4f(seg.w + e, make_float4(ww[0], ww[1], ww[2], ww[3]));
+  st4f(seg.m + e, make_float4(mm[0], mm[1], mm[2], mm[3]));
+  st4f(seg.v + e, make_float4(vv[0], vv[1], vv[2], vv[3]));
+  if constexpr (ODT != MB_NONE) store4<ODT>(seg.out, e, ww);
+}
+
+template <int GDT, int ODT>
+__device__ __forceinline__ void apply_scalar(const mb_segment& seg, int64_t e, int64_t end,
+                                             const StepScalars& s, const GradPrep& prep) {
+  for (; e < end; ++e) {
+    float w = seg.w[e], m = seg.m[e], v = seg.v[e];
+    adam_elem(w, m, v, prep(load1<GDT>(seg.g, e)), s);
+    seg.w[e] = w;
+    seg.m[e] = m;
+    seg.v[e] = v;
+    if constexpr (ODT != MB_NONE) store1<ODT>(seg.out, e, w);
+  }
+}
+
+__device__ __forceinline__ bool seg_vec_ok(const mb_segment& seg, int gdt, int odt) {
+  bool ok = aligned(seg.w, 16) && aligned(seg.m, 16) && aligned(seg.v, 16);
+  ok = ok && aligned(seg.g, gdt == MB_F32 ? 16 : 8);
+  if (odt != MB_NONE) ok = ok && aligned(seg.out, 8);
+  return ok;
+}
+
+// Process one tile of one segment: two coalesced sweeps of 1024 elements.
+template <int GDT, int ODT>
+__device__ __forceinline__ void apply_tile(const mb_segment& seg, int64_t tile_in_seg, bool vec,
+                                           const StepScalars& s, const GradPrep& prep) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    int64_t e = tile_in_seg * kTile + h * kHalf + threadIdx.x * kQuad;
+    if (e >= seg.numel) continue;
+    int64_t end = e + kQuad < seg.numel ? e + kQuad : seg.numel;
+    if (vec && end - e == kQuad) apply_quad<GDT, ODT>(seg, e, s, prep);
+    else apply_scalar<GDT, ODT>(seg, e, end, s, prep);
+  }
+}
+
+// Kernel 1 (plan mode): every segment's scalars come from the finalize.
+template <int GDT, int ODT>
+__global__ void __launch_bounds__(kThreads) k_adamw_apply(ApplyArgs a) {
+  const mb_step_state* st = a.state;
+  if (st->skip) return;
+  GradPrep prep = make_prep(__double2float_rn(st->step_scale), st->clip_coef);
+  int cur = -1;
+  mb_segment seg;
+  StepScalars s;
+  bool vec = false;
+  for (int64_t tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
+    int si = cur < 0 ? find_segment(a.segs, a.n_segs, tile) : cur;
+    while (si + 1 < a.n_segs && __ldg(&a.segs[si + 1].tile_begin) <= tile) ++si;
+    if (si != cur) {
+      cur = si;
+      seg = a.segs[si];
+      s = group_scalars(a.groups[seg.group], a.seg_scal[si]);
+      vec = seg_vec_ok(seg, GDT, ODT);
+    }
+    apply_tile<GDT, ODT>(seg, tile - seg.tile_begin, vec, s, prep);
+  }
+}
+
+// Kernel 1 (single tensor, host scalars): DiskState.update on device memory.
+template <int GDT, int ODT>
+__global__ void __launch_bounds__(kThreads) k_adamw_update(mb_segment seg, int64_t n_tiles,
+                                                            mb_host_scalars hs) {
+  StepScalars s;
+  s.small = fabsf(hs.omb1) < 0.5f;
+  s.lw = s.small ? hs.omb1 : __fsub_rn(hs.omb1, 1.0f);
+  s.cwd = hs.cwd; s.b2 = hs.beta2; s.omb2 = hs.omb2; s.eps = hs.eps; s.nss = hs.nss; s.bc2s = hs.bc2s;
+  GradPrep prep = make_prep(hs.scale, hs.coef);
+  bool vec = seg_vec_ok(seg, GDT, ODT);
+  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) apply_tile<GDT, ODT>(seg, tile, vec, s, prep);
+}
+
+// ------------------------------------------------------------- kernel 2 --
+
+struct StatsArgs {
+  const mb_segment* segs;
+  int64_t n_tiles;
+  int32_t n_segs;
+  mb_adamw_plan plan;      // for the fused finalize
+  mb_finalize_opts fin;
+  int32_t fuse_finalize;
+  int32_t unscale;         // divide by state.scale
+};
+
+__device__ __forceinline__ void accum(float x, const GradPrep& prep, double& acc, double& bad) {
+  if (!is_finite(x)) bad += 1.0;
+  float y = prep(x);
+  double d = (double)y;
+  acc = __fma_rn(d, d, acc);
+}
+
+// Block-wide sum of (a, b) in a fixed order; result valid in thread 0.
+__device__ __forceinline__ double2 block_sum2(double a, double b) {
+  __shared__ double2 red[kThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_down_sync(0xffffffffu, a, o);
+    b += __shfl_down_sync(0xffffffffu, b, o);
+  }
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = make_double2(a, b);
+  __syncthreads();
+  double2 r = make_double2(0.0, 0.0);
+  if (warp == 0) {
+    r = lane < kThreads / 32 ? red[lane] : make_double2(0.0, 0.0);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      r.x += __shfl_down_sync(0xffffffffu, r.x, o);
+      r.y += __shfl_down_sync(0xffffffffu, r.y, o);
+    }
+  }
+  __syncthreads();
+  return r;
+}
+
+// Loss-scale transition, skip decision, clip coefficient (thread 0), then clock
+// advance and per-segment scalars (all threads). One CTA runs this.
+__device__ void finalize_block(const mb_adamw_plan& p, const mb_finalize_opts& f) {
+  __shared__ int s_skip;
+  mb_step_state* st = p.state;
+  if (threadIdx.x == 0) {
+    double sumsq = st->sumsq;
+    bool found = st->nonfinite != 0.0 || !isfinite(sumsq);
+    int skip = 0, status = MB_OK;
+    double used = (f.flags & MB_FIN_LOSS_SCALE) ? st->scale : 1.0;
+    if (f.flags & MB_FIN_LOSS_SCALE) {
+      if (found) {
+        skip = 1;
+        if (st->scale <= 1.0) {
+          status = MB_ERR_OVERFLOW_MIN_SCALE;  // precision.py:10: state unchanged
+        } else {
+          st->scale = fmax(1.0, st->scale * f.backoff);  // precision.py:11
+          st->good_steps = 0;
+        }
+      } else {
+        st->good_steps += 1;  // precision.py:13-14
+        if (st->good_steps >= st->growth_interval) {
+          st->scale = fmin(st->scale * f.growth, st->max_scale);
+          st->good_steps = 0;
+        }
+      }
+    } else if (found && (f.flags & MB_FIN_GATE)) {
+      skip = 1;
+      status = MB_ERR_NONFINITE;  // optimizer.py:50-51
+    }
+    double norm = sqrt(sumsq);
+    float coef = 1.0f;
+    if (!skip && (f.flags & MB_FIN_CLIP_TORCH)) {
+      // clip_grad.py:165-169: (norm + 1e-6).reciprocal() * max_norm, clamp(max=1)
+      float t = __fadd_rn(__double2float_rn(norm), 1e-6f);
+      float c = __fmul_rn(__frcp_rn(t), __double2float_rn(f.max_norm));
+      coef = c < 1.0f ? c : 1.0f;
+    } else if (!skip && (f.flags & MB_FIN_CLIP_DISK)) {
+      double c = fmin(1.0, f.max_norm / (norm + 1e-6));  // disk.py:489
+      coef = __double2float_rn(c);
+    }
+    st->norm = norm;
+    st->step_scale = used;
+    st->clip_coef = coef;
+    st->skip = skip;
+    st->status = status;
+    if (skip) st->steps_skipped += 1; else st->steps_applied += 1;
+    s_skip = skip;
+  }
+  __syncthreads();
+  float2* seg_scal = reinterpret_cast<float2*>(static_cast<char*>(p.workspace) + kSegScalOffset);
+  for (int i = threadIdx.x; i < p.n_segs; i += blockDim.x) {
+    mb_segment seg = p.segs[i];
+    int32_t t = p.clocks[seg.clock];
+    if (!s_skip) {
+      t += 1;
+      p.clocks[seg.clock] = t;
+    }
+    mb_group g = p.groups[seg.group];
+    int64_t tt = t < p.bc_len ? t : p.bc_len - 1;
+    if (tt < 0) tt = 0;
+    double bc1 = p.bc[(2 * (int64_t)g.table) * p.bc_len + tt];
+    double bc2s = p.bc[(2 * (int64_t)g.table + 1) * p.bc_len + tt];
+    seg_scal[i] = make_float2(__double2float_rn(-(g.lr / bc1)), __double2float_rn(bc2s));
+  }
+}
+
+template <int GDT>
+__global__ void __launch_bounds__(kThreads) k_grad_stats(StatsArgs a) {
+  mb_step_state* st = a.plan.state;
+  float scale = a.unscale ? __double2float_rn(st->scale) : 1.0f;
+  GradPrep prep = make_prep(scale, 1.0f);
+  double acc = 0.0, bad = 0.0;
+  int cur = -1;
+  mb_segment seg;
+  bool vec = false;
+  for (int64_t tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
+    int si = cur < 0 ? find_segment(a.segs, a.n_segs, tile) : cur;
+    while (si + 1 < a.n_segs && __ldg(&a.segs[si + 1].tile_begin) <= tile) ++si;
+    if (si != cur) {
+      cur = si;
+      seg = a.segs[si];
+      vec = aligned(seg.g, GDT == MB_F32 ? 16 : 8);
+    }
+    int64_t base = (tile - seg.tile_begin) * kTile + threadIdx.x * kQuad;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int64_t e = base + h * kHalf;
+      if (e >= seg.numel) continue;
+      if (vec && e + kQuad <= seg.numel) {
+        float x[4];
+        load4<GDT>(seg.g, e, x);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) accum(x[j], prep, acc, bad);
+      } else {
+        int64_t end = e + kQuad < seg.numel ? e + kQuad : seg.numel;
+        for (; e < end; ++e) accum(load1<GDT>(seg.g, e), prep, acc, bad);
+      }
+    }
+  }
+  double2 r = block_sum2(acc, bad);
+  char* ws = static_cast<char*>(a.plan.workspace);
+  double2* partials = reinterpret_cast<double2*>(ws);
+  unsigned int* ticket = reinterpret_cast<unsigned int*>(ws + kTicketOffset);
+  __shared__ unsigned int s_last;
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = r;
+    __threadfence();
+    s_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // Last CTA: fixed-order reduction of the partials (deterministic for a grid).
+  double a0 = 0.0, b0 = 0.0;
+  for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
+    double2 q = __ldcg(&partials[i]);
+    a0 += q.x;
+    b0 += q.y;
+  }
+  double2 tot = block_sum2(a0, b0);
+  if (threadIdx.x == 0) {
+    st->sumsq = tot.x;
+    st->nonfinite = tot.y;
+    *ticket = 0u;
+  }
+  __syncthreads();
+  if (a.fuse_finalize) {
+    __threadfence_block();
+    finalize_block(a.plan, a.fin);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_step_finalize(mb_adamw_plan p, mb_finalize_opts f) {
+  finalize_block(p, f);
+}
+
+// ----------------------------------------------------------- dispatch ----
+
+using ApplyFn = void (*)(ApplyArgs);
+using UpdateFn = void (*)(mb_segment, int64_t, mb_host_scalars);
+
+template <int GDT>
+ApplyFn pick_apply(int odt) {
+  switch (odt) {
+    case MB_NONE: return &k_adamw_apply<GDT, MB_NONE>;
+    case MB_F16: return &k_adamw_apply<GDT, MB_F16>;
+    case MB_BF16: return &k_adamw_apply<GDT, MB_BF16>;
+    default: return nullptr;
+  }
+}
+ApplyFn pick_apply(int gdt, int odt) {
+  switch (gdt) {
+    case MB_F32: return pick_apply<MB_F32>(odt);
+    case MB_F16: return pick_apply<MB_F16>(odt);
+    case MB_BF16: return pick_apply<MB_BF16>(odt);
+    default: return nullptr;
+  }
+}
+template <int GDT>
+UpdateFn pick_update(int odt) {
+  switch (odt) {
+    case MB_NONE: return &k_adamw_update<GDT, MB_NONE>;
+    case MB_F16: return &k_adamw_update<GDT, MB_F16>;
+    case MB_BF16: return &k_adamw_update<GDT, MB_BF16>;
+    default: return nullptr;
+  }
+}
+UpdateFn pick_update(int gdt, int odt) {
+  switch (gdt) {
+    case MB_F32: return pick_update<MB_F32>(odt);
+    case MB_F16: return pick_update<MB_F16>(odt);
+    case MB_BF16: return pick_update<MB_BF16>(odt);
+    default: return nullptr;
+  }
+}
+using StatsFn = void (*)(StatsArgs);
+StatsFn pick_stats(int gdt) {
+  switch (gdt) {
+    case MB_F32: return &k_grad_stats<MB_F32>;
+    case MB_F16: return &k_grad_stats<MB_F16>;
+    case MB_BF16: return &k_grad_stats<MB_BF16>;
+    default: return nullptr;
+  }
+}
+
+int check_plan(const mb_adamw_plan* p) {
+  if (!p || !p->segs || !p->groups || !p->bc || !p->clocks || !p->workspace || !p->state) return MB_ERR_ARG;
+  if (p->n_segs <= 0 || p->n_groups <= 0 || p->n_tiles <= 0 || p->bc_len <= 0) return MB_ERR_ARG;
+  if (p->grad_dtype < MB_F32 || p->grad_dtype > MB_BF16) return MB_ERR_ARG;
+  if (p->out_dtype != MB_NONE && p->out_dtype != MB_F16 && p->out_dtype != MB_BF16) return MB_ERR_ARG;
+  if (!aligned(p->workspace, 256) || !aligned(p->state, 16)) return MB_ERR_ALIGN;
+  return MB_OK;
+}
+
+int check_fin(const mb_finalize_opts* f) {
+  if (!f) return MB_ERR_ARG;
+  if (f->flags & ~(MB_FIN_LOSS_SCALE | MB_FIN_GATE | MB_FIN_CLIP_TORCH | MB_FIN_CLIP_DISK)) return MB_ERR_ARG;
+  if ((f->flags & MB_FIN_CLIP_TORCH) && (f->flags & MB_FIN_CLIP_DISK)) return MB_ERR_ARG;
+  if ((f->flags & (MB_FIN_CLIP_TORCH | MB_FIN_CLIP_DISK)) && !(f->max_norm > 0)) return MB_ERR_ARG;
+  if ((f->flags & MB_FIN_LOSS_SCALE) && !(f->backoff > 0 && f->growth >= 1)) return MB_ERR_ARG;
+  return MB_OK;
+}
+
+int launch_status() { return cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA; }
+
+}  // namespace
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" {
+
+MB_API int mb_version(void) { return 1; }
+
+MB_API const char* mb_status_string(int status) {
+  switch (status) {
+    case MB_OK: return "ok";
+    case MB_ERR_ARG: return "invalid argument";
+    case MB_ERR_ALIGN: return "misaligned pointer";
+    case MB_ERR_CUDA: return "CUDA error";
+    case MB_ERR_OVERFLOW_MIN_SCALE: return "FP16 overflow at minimum loss scale; state unchanged";
+    case MB_ERR_NONFINITE: return "nonfinite gradient; optimizer not updated";
+    case MB_ERR_TIMEOUT: return "bounded wait expired";
+    case MB_ERR_INDEX: return "row index out of range";
+    case MB_ERR_UNREPRESENTABLE: return "weights cannot be represented by finite FP16";
+    default: return "unknown status";
+  }
+}
+
+MB_API int mb_segments_plan(mb_segment* segs, int32_t n, int64_t* n_tiles) {
+  if (!segs || n <= 0 || !n_tiles) return MB_ERR_ARG;
+  int64_t t = 0;
+  for (int32_t i = 0; i < n; ++i) {
+    if (segs[i].numel <= 0 || !segs[i].w || !segs[i].m || !segs[i].v || !segs[i].g) return MB_ERR_ARG;
+    segs[i].tile_begin = t;
+    t += (segs[i].numel + kTile - 1) / kTile;
+  }
+  *n_tiles = t;
+  return MB_OK;
+}
+
+MB_API size_t mb_workspace_bytes(int32_t n_segs) { return workspace_bytes(n_segs); }
+
+MB_API int mb_step_state_init(mb_step_state* s, double scale, int64_t growth_interval) {
+  if (!s || !(scale > 0) || growth_interval <= 0) return MB_ERR_ARG;
+  *s = mb_step_state{};
+  s->scale = scale;
+  s->step_scale = 1.0;
+  s->growth_interval = growth_interval;
+  s->max_scale = 65536.0;
+  s->clip_coef = 1.0f;
+  return MB_OK;
+}
+
+MB_API int mb_grad_stats(const mb_adamw_plan* p, const mb_finalize_opts* fin, mb_stream_t stream) {
+  int rc = check_plan(p);
+  if (rc) return rc;
+  if (fin && (rc = check_fin(fin))) return rc;
+  StatsFn fn = pick_stats(p->grad_dtype);
+  StatsArgs a;
+  a.segs = p->segs;
+  a.n_tiles = p->n_tiles;
+  a.n_segs = p->n_segs;
+  a.plan = *p;
+  a.fin = fin ? *fin : mb_finalize_opts{};
+  a.fuse_finalize = fin != nullptr;
+  a.unscale = fin ? (fin->flags & MB_FIN_LOSS_SCALE) != 0 : 0;
+  int grid = grid_for(reinterpret_cast<const void*>(fn), p->n_tiles);
+  if (grid > kMaxStatsBlocks) grid = kMaxStatsBlocks;
+  fn<<<grid, kThreads, 0, (cudaStream_t)stream>>>(a);
+  return launch_status();
+}
+
+MB_API int mb_step_finalize(const mb_adamw_plan* p, const mb_finalize_opts* fin, mb_stream_t stream) {
+  int rc = check_plan(p);
+  if (rc) return rc;
+  if ((rc = check_fin(fin))) return rc;
+  k_step_finalize<<<1, kThreads, 0, (cudaStream_t)stream>>>(*p, *fin);
+  return launch_status();
+}
+
+MB_API int mb_adamw_apply(const mb_adamw_plan* p, mb_stream_t stream) {
+  int rc = check_plan(p);
+  if (rc) return rc;
+  ApplyFn fn = pick_apply(p->grad_dtype, p->out_dtype);
+  if (!fn) return MB_ERR_ARG;
+  ApplyArgs a;
+  a.segs = p->segs;
+  a.groups = p->groups;
+  a.seg_scal = reinterpret_cast<const float2*>(static_cast<const char*>(p->workspace) + kSegScalOffset);
+  a.state = p->state;
+  a.n_tiles = p->n_tiles;
+  a.n_segs = p->n_segs;
+  int grid = grid_for(reinterpret_cast<const void*>(fn), p->n_tiles);
+  fn<<<grid, kThreads, 0, (cudaStream_t)stream>>>(a);
+  return launch_status();
+}
+
+MB_API int mb_adamw_step(const mb_adamw_plan* p, const mb_finalize_opts* fin, mb_stream_t stream) {
+  int rc = mb_grad_stats(p, fin, stream);
+  if (rc) return rc;
+  return mb_adamw_apply(p, stream);
+}
+
+MB_API int mb_adamw_update(float* w, float* m, float* v, const void* g, int32_t gdt, void* out,
+                           int32_t odt, int64_t numel, const mb_host_scalars* s, mb_stream_t stream) {
+  if (!w || !m || !v || !g || !s || numel < 0) return MB_ERR_ARG;
+  if (odt != MB_NONE && !out) return MB_ERR_ARG;
+  UpdateFn fn = pick_update(gdt, odt);
+  if (!fn) return MB_ERR_ARG;
+  if (numel == 0) return MB_OK;
+  mb_segment seg{};
+  seg.w = w; seg.m = m; seg.v = v; seg.g = g; seg.out = out; seg.numel = numel;
+  int64_t tiles = (numel + kTile - 1) / kTile;
+  int grid = grid_for(reinterpret_cast<const void*>(fn), tiles);
+  fn<<<grid, kThreads, 0, (cudaStream_t)stream>>>(seg, tiles, *s);
+  return launch_status();
+}
+
+}  // extern "C"

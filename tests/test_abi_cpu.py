@@ -1,0 +1,60 @@
+"""The C-ABI library loads on a host without a GPU and exports every entry
+point that include/morph_b200.h declares (no compute calls here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from morph_b200 import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    text = open(os.path.join(REPO, "include", "morph_b200.h")).read()
+    return sorted(set(re.findall(r"MB_API\s+[\w\s\*]+?\b(mb_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_bound_surface():
+    declared = declared_symbols()
+    assert declared, "no MB_API declarations found"
+    assert set(declared) == set(_lib.SIGNATURES), (set(declared) ^ set(_lib.SIGNATURES))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = _lib.lib()
+    for name in declared_symbols():
+        assert hasattr(L, name), name
+        assert ctypes.cast(getattr(L, name), ctypes.c_void_p).value
+
+
+def test_host_only_entry_points():
+    L = _lib.lib()
+    assert L.mb_version() >= 1
+    assert _lib.status_string(_lib.MB_ERR_NONFINITE).startswith("nonfinite gradient")
+    st = _lib.StepState()
+    assert L.mb_step_state_init(ctypes.byref(st), 65536.0, 2000) == 0
+    assert st.scale == 65536.0 and st.growth_interval == 2000 and st.clip_coef == 1.0
+    assert L.mb_step_state_init(ctypes.byref(st), 0.0, 2000) == _lib.MB_ERR_ARG
+    segs = (_lib.Segment * 3)()
+    for i, n in enumerate((1, 2048, 2049)):
+        segs[i].w = segs[i].m = segs[i].v = segs[i].g = 4096
+        segs[i].numel = n
+    tiles = ctypes.c_int64(0)
+    assert L.mb_segments_plan(segs, 3, ctypes.byref(tiles)) == 0
+    assert [s.tile_begin for s in segs] == [0, 1, 2] and tiles.value == 4
+    assert L.mb_workspace_bytes(10) % 256 == 0
+
+
+def test_status_codes_map_to_reference_exceptions():
+    with pytest.raises(FloatingPointError):
+        _lib.check(_lib.MB_ERR_OVERFLOW_MIN_SCALE)
+    with pytest.raises(FloatingPointError):
+        _lib.check(_lib.MB_ERR_NONFINITE)
+    with pytest.raises(ValueError):
+        _lib.check(_lib.MB_ERR_ARG)
+    with pytest.raises(IndexError):
+        _lib.check(_lib.MB_ERR_INDEX)
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.MB_ERR_CUDA)
