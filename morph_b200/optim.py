@@ -108,6 +108,7 @@ class StepEngine:
         self.tables = BiasCorrectionTables(self.device)
         self.slots: dict[int, int] = {}
         self.clocks = torch.zeros(0, dtype=torch.int32, device=self.device)
+        self.generation = 0
         self.max_clock = 0
         self.loss_scale = loss_scale
         if loss_scale is not None:
@@ -126,21 +127,30 @@ class StepEngine:
         self._groups_dev = None
 
     # -- clocks ------------------------------------------------------------------
+    def reserve(self, n: int) -> None:
+        """Grow the clock array to at least n slots. Growing moves it, so views
+        handed out by clock_view() before a growth must be refreshed
+        (``generation`` changes when that happens)."""
+        if n > self.clocks.numel():
+            grown = torch.zeros(max(16, n, 2 * self.clocks.numel()), dtype=torch.int32, device=self.device)
+            grown[: self.clocks.numel()] = self.clocks
+            self.clocks = grown
+            self.generation += 1
+            self._seg_key = None
+
     def slot(self, p: torch.Tensor, initial_clock: int = 0) -> int:
         key = id(p)
         if key not in self.slots:
             s = len(self.slots)
+            self.reserve(s + 1)
             self.slots[key] = s
-            if s >= self.clocks.numel():
-                grown = torch.zeros(max(16, 2 * self.clocks.numel()), dtype=torch.int32, device=self.device)
-                grown[: self.clocks.numel()] = self.clocks
-                self.clocks = grown
             self.clocks[s] = int(initial_clock)
             self.max_clock = max(self.max_clock, int(initial_clock))
         return self.slots[key]
 
     def set_clock(self, p, value: int) -> None:
-        self.clocks[self.slot(p)] = int(value)
+        s = self.slot(p)
+        self.clocks[s] = int(value)
         self.max_clock = max(self.max_clock, int(value))
 
     def clock_view(self, p) -> torch.Tensor:
@@ -244,11 +254,14 @@ class AdamW(torch.optim.Optimizer):
         self.sync = gate if sync is None else sync
         self.low_precision_copies: dict[torch.Tensor, torch.Tensor] = {}
         self._engine: StepEngine | None = None
+        self._generation = 0
 
     # -- helpers ---------------------------------------------------------------------
     def _engine_for(self, device) -> StepEngine:
         if self._engine is None:
             self._engine = StepEngine(device, self.loss_scale)
+            self._engine.reserve(sum(len(g["params"]) for g in self.param_groups))
+            self._generation = self._engine.generation
         elif self._engine.device != device:
             raise ValueError("all parameters of one AdamW must live on one CUDA device")
         return self._engine
@@ -313,6 +326,11 @@ class AdamW(torch.optim.Optimizer):
         if not entries:
             return loss
         eng = self._engine_for(device)
+        if eng.generation != self._generation:  # the clock array moved: refresh the step views
+            for p, st in self.state.items():
+                if id(p) in eng.slots:
+                    st["step"] = eng.clock_view(p)
+            self._generation = eng.generation
         odt = _lib.dtype_code(self.low_precision) if self.low_precision is not None else _lib.MB_NONE
         with torch.cuda.device(device):
             eng.step(entries, groups, gdt, odt, self._fin_flags(), self.max_norm)
