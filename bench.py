@@ -43,13 +43,15 @@ STATS_BYTES = 2    # kernel 2: g 2 R
 FALLBACK_HBM_GBS = 6650.0
 
 
-def config2_shapes():
+def config2_shapes(layers=42, embedding=True):
+    """Config 2's tensors; ``layers``/``embedding`` shrink it for profiling captures."""
     shapes = []
-    for layer in range(42):
+    for layer in range(layers):
         shapes += [(f"blocks.{layer}.ffn.{n}", (3072, 6144)) for n in ("gate", "up", "down")]
         shapes += [(f"blocks.{layer}.ssm.{n}", (3072, 3072)) for n in ("in", "x", "z", "out")]
         shapes += [(f"blocks.{layer}.vec.{n}", (3072,)) for n in ("norm", "bias", "dt_bias", "skip")]
-    shapes.append(("embedding.weight", (65536, 3072)))
+    if embedding:
+        shapes.append(("embedding.weight", (65536, 3072)))
     return shapes
 
 
@@ -198,7 +200,7 @@ def run_morph(args, rank, world, local_rank):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    shapes = config2_shapes()
+    shapes = config2_shapes(args.layers, not args.no_embedding)
     sizes = [numel(s) for _, s in shapes]
     total = sum(sizes)
     lo, hi = shard_bounds(total, world, rank)
@@ -309,8 +311,10 @@ def run_morph(args, rank, world, local_rank):
         "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2: dense 5B-shaped AdamW step (4,165,459,968 params, BF16 grads, "
-                               "clip 1.0, BF16 compute copy)",
+        "config": {"workload": ("config2: dense 5B-shaped AdamW step (4,165,459,968 params, BF16 grads, "
+                                "clip 1.0, BF16 compute copy)") if total == 4165459968 else
+                               f"config2 reduced for profiling: {args.layers} layers"
+                               f"{'' if not args.no_embedding else ', no embedding'} ({total:,} params)",
                    "params": total, "grad_dtype": "bf16", "parallelism": f"zero1-dp{world}",
                    "l2": "inputs larger than L2 (116.6 GB of traffic per step vs 126 MB L2); no flush"},
         "hbm_gbs": (APPLY_BYTES + STATS_BYTES) * total / (ms_per_step / 1e3) / 1e9,
@@ -387,6 +391,8 @@ def main():
     ap.add_argument("--impl", choices=["morph", "reference"], default="morph")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=42, help="profiling only: fewer layers than config 2")
+    ap.add_argument("--no-embedding", action="store_true", help="profiling only: drop the embedding")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "morph":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

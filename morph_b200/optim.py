@@ -355,16 +355,25 @@ class AdamW(torch.optim.Optimizer):
 
     # -- checkpoints in torch's CPU layout ----------------------------------------
     def state_dict(self):
-        swapped = {}
-        for p, st in self.state.items():
-            if torch.is_tensor(st.get("step")) and st["step"].is_cuda:
-                swapped[p] = st["step"]
-                st["step"] = torch.tensor(float(st["step"].item()), dtype=torch.float32)
-        try:
-            return super().state_dict()
-        finally:
-            for p, view in swapped.items():
-                self.state[p]["step"] = view
+        """torch's layout: per-parameter ``step`` as a 0-dim float32 CPU tensor
+        (one device read of all clocks), ``exp_avg``/``exp_avg_sq`` as stored."""
+        sd = super().state_dict()
+        clocks = self._engine.clocks.cpu() if self._engine is not None else None
+        index = {}
+        for group, packed in zip(self.param_groups, sd["param_groups"]):
+            for p, i in zip(group["params"], packed["params"]):
+                index[i] = p
+        state = {}
+        for i, st in sd["state"].items():
+            st = dict(st)  # never hand out the live per-parameter dict
+            step = st.get("step")
+            if torch.is_tensor(step) and step.is_cuda:
+                p = index[i]
+                value = int(clocks[self._engine.slots[id(p)]]) if id(p) in self._engine.slots else int(step.item())
+                st["step"] = torch.tensor(float(value), dtype=torch.float32)
+            state[i] = st
+        sd["state"] = state
+        return sd
 
     def load_state_dict(self, state_dict):
         super().load_state_dict(state_dict)

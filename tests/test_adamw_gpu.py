@@ -160,12 +160,14 @@ def test_fused_clip_matches_reference_rules(cuda, mode):
         assert abs(got["norm"] - norm) <= 1e-12 * max(norm, 1.0)
         assert abs(np.float32(got["clip_coef"]) - want) <= np.spacing(want)
         if mode == "torch":  # against torch's own clip_grad_norm_ on the CPU
+            # a one-element probe gradient 2**-60 (negligible in the norm) reads
+            # torch's applied coefficient back exactly: probe * coef * 2**60
             ref = [torch.nn.Parameter(torch.zeros(s)) for s in shapes] + [torch.nn.Parameter(torch.zeros(1))]
             for q, g in zip(ref, bf):
                 q.grad = g.float().reshape(q.shape)
-            ref[-1].grad = torch.ones(1)
-            tn = torch.nn.utils.clip_grad_norm_(ref, 1.0)
-            tcoef = float(ref[-1].grad[0]) if float(tn) > 1 else 1.0
+            ref[-1].grad = torch.full((1,), 2.0 ** -60)
+            torch.nn.utils.clip_grad_norm_(ref, 1.0)
+            tcoef = float(ref[-1].grad[0]) * 2.0 ** 60
             assert abs(got["clip_coef"] - tcoef) <= 2e-6 * tcoef
         coef = np.float32(got["clip_coef"])
         for i, p in enumerate(params):
