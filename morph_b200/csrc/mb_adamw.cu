@@ -22,6 +22,12 @@
 
 #include "mb_common.cuh"
 
+// Compile-time tuning knob: minimum resident CTAs per SM requested from ptxas
+// for kernel 1 (caps its registers per thread).
+#ifndef MB_APPLY_MIN_BLOCKS
+#define MB_APPLY_MIN_BLOCKS 1
+#endif
+
 namespace mb {
 
 int persistent_blocks(const void* kernel, int threads, size_t smem) {
@@ -111,12 +117,42 @@ __device__ __forceinline__ bool seg_vec_ok(const mb_segment& seg, int gdt, int o
 }
 
 // Process one tile of one segment: two coalesced sweeps of 1024 elements.
+// When both of a thread's quads are in range, all eight loads are issued
+// before any arithmetic or store (112 B in flight per thread for BF16 grads).
 template <int GDT, int ODT>
 __device__ __forceinline__ void apply_tile(const mb_segment& seg, int64_t tile_in_seg, bool vec,
                                            const StepScalars& s, const GradPrep& prep) {
+  const int64_t e0 = tile_in_seg * kTile + threadIdx.x * kQuad;
+  const int64_t e1 = e0 + kHalf;
+  if (vec && e1 + kQuad <= seg.numel) {
+    float g0[4], g1[4];
+    load4<GDT>(seg.g, e0, g0);
+    load4<GDT>(seg.g, e1, g1);
+    float4 w0 = ld4f(seg.w + e0), w1 = ld4f(seg.w + e1);
+    float4 m0 = ld4f(seg.m + e0), m1 = ld4f(seg.m + e1);
+    float4 v0 = ld4f(seg.v + e0), v1 = ld4f(seg.v + e1);
+    float wa[4] = {w0.x, w0.y, w0.z, w0.w}, ma[4] = {m0.x, m0.y, m0.z, m0.w}, va[4] = {v0.x, v0.y, v0.z, v0.w};
+    float wb[4] = {w1.x, w1.y, w1.z, w1.w}, mb_[4] = {m1.x, m1.y, m1.z, m1.w}, vb[4] = {v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      adam_elem(wa[j], ma[j], va[j], prep(g0[j]), s);
+      adam_elem(wb[j], mb_[j], vb[j], prep(g1[j]), s);
+    }
+    st4f(seg.w + e0, make_float4(wa[0], wa[1], wa[2], wa[3]));
+    st4f(seg.m + e0, make_float4(ma[0], ma[1], ma[2], ma[3]));
+    st4f(seg.v + e0, make_float4(va[0], va[1], va[2], va[3]));
+    st4f(seg.w + e1, make_float4(wb[0], wb[1], wb[2], wb[3]));
+    st4f(seg.m + e1, make_float4(mb_[0], mb_[1], mb_[2], mb_[3]));
+    st4f(seg.v + e1, make_float4(vb[0], vb[1], vb[2], vb[3]));
+    if constexpr (ODT != MB_NONE) {
+      store4<ODT>(seg.out, e0, wa);
+      store4<ODT>(seg.out, e1, wb);
+    }
+    return;
+  }
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    int64_t e = tile_in_seg * kTile + h * kHalf + threadIdx.x * kQuad;
+    int64_t e = h ? e1 : e0;
     if (e >= seg.numel) continue;
     int64_t end = e + kQuad < seg.numel ? e + kQuad : seg.numel;
     if (vec && end - e == kQuad) apply_quad<GDT, ODT>(seg, e, s, prep);
@@ -126,7 +162,7 @@ __device__ __forceinline__ void apply_tile(const mb_segment& seg, int64_t tile_i
 
 // Kernel 1 (plan mode): every segment's scalars come from the finalize.
 template <int GDT, int ODT>
-__global__ void __launch_bounds__(kThreads) k_adamw_apply(ApplyArgs a) {
+__global__ void __launch_bounds__(kThreads, MB_APPLY_MIN_BLOCKS) k_adamw_apply(ApplyArgs a) {
   const mb_step_state* st = a.state;
   if (st->skip) return;
   GradPrep prep = make_prep(__double2float_rn(st->step_scale), st->clip_coef);
@@ -171,13 +207,6 @@ struct StatsArgs {
   int32_t fuse_finalize;
   int32_t unscale;         // divide by state.scale
 };
-
-__device__ __forceinline__ void accum(float x, const GradPrep& prep, double& acc, double& bad) {
-  if (!is_finite(x)) bad += 1.0;
-  float y = prep(x);
-  double d = (double)y;
-  acc = __fma_rn(d, d, acc);
-}
 
 // Block-wide sum of (a, b) in a fixed order; result valid in thread 0.
 __device__ __forceinline__ double2 block_sum2(double a, double b) {
@@ -270,45 +299,112 @@ __device__ void finalize_block(const mb_adamw_plan& p, const mb_finalize_opts& f
   }
 }
 
+// Kernel 2. Each CTA owns a contiguous run of tiles and reads it with one
+// 16-byte load per thread per tile (8 BF16/FP16 or 4+4 FP32 elements), four
+// tiles in flight per iteration. Squares are accumulated in FP64; a nonfinite
+// gradient makes the FP64 sum nonfinite (finite squares cannot overflow it:
+// 2^33 elements x FLT_MAX^2 < DBL_MAX), so finiteness is tested once per
+// partial instead of per element.
 template <int GDT>
-__global__ void __launch_bounds__(kThreads) k_grad_stats(StatsArgs a) {
-  mb_step_state* st = a.plan.state;
-  float scale = a.unscale ? __double2float_rn(st->scale) : 1.0f;
-  GradPrep prep = make_prep(scale, 1.0f);
-  double acc = 0.0, bad = 0.0;
-  int cur = -1;
-  mb_segment seg;
-  bool vec = false;
-  for (int64_t tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
-    int si = cur < 0 ? find_segment(a.segs, a.n_segs, tile) : cur;
-    while (si + 1 < a.n_segs && __ldg(&a.segs[si + 1].tile_begin) <= tile) ++si;
-    if (si != cur) {
-      cur = si;
-      seg = a.segs[si];
-      vec = aligned(seg.g, GDT == MB_F32 ? 16 : 8);
+__device__ __forceinline__ void stats_elems(const uint4& q, bool unscale, const GradPrep& prep, double& acc) {
+  float x[8];
+  int n = 8;
+  if (GDT == MB_BF16) {
+    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      x[2 * j] = __uint_as_float(u[j] << 16);
+      x[2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
     }
-    int64_t base = (tile - seg.tile_begin) * kTile + threadIdx.x * kQuad;
+  } else if (GDT == MB_F16) {
+    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      int64_t e = base + h * kHalf;
-      if (e >= seg.numel) continue;
-      if (vec && e + kQuad <= seg.numel) {
-        float x[4];
-        load4<GDT>(seg.g, e, x);
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[j]));
+      x[2 * j] = f.x;
+      x[2 * j + 1] = f.y;
+    }
+  } else {
+    x[0] = __uint_as_float(q.x); x[1] = __uint_as_float(q.y);
+    x[2] = __uint_as_float(q.z); x[3] = __uint_as_float(q.w);
+    n = 4;
+  }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) accum(x[j], prep, acc, bad);
-      } else {
-        int64_t end = e + kQuad < seg.numel ? e + kQuad : seg.numel;
-        for (; e < end; ++e) accum(load1<GDT>(seg.g, e), prep, acc, bad);
+  for (int j = 0; j < 8; ++j) {
+    if (j < n) {
+      float y = unscale ? prep(x[j]) : x[j];
+      double d = (double)y;
+      acc = __fma_rn(d, d, acc);
+    }
+  }
+}
+
+template <int GDT, bool UNSCALE>
+__global__ void __launch_bounds__(kThreads) k_grad_stats(StatsArgs a) {
+  constexpr int kU = 4;                                  // tiles in flight per iteration
+  constexpr int kEpl = GDT == MB_F32 ? 4 : 8;            // elements per 16-byte load
+  constexpr int kLoads = (kTile / kThreads) / kEpl;      // 16-byte loads per thread per tile
+  using T = typename Elem<GDT>::T;
+  mb_step_state* st = a.plan.state;
+  GradPrep prep = make_prep(UNSCALE ? __double2float_rn(st->scale) : 1.0f, 1.0f);
+  double acc = 0.0;
+  const int64_t per = (a.n_tiles + gridDim.x - 1) / gridDim.x;
+  const int64_t t0 = (int64_t)blockIdx.x * per;
+  const int64_t t1 = t0 + per < a.n_tiles ? t0 + per : a.n_tiles;
+  int si = t0 < a.n_tiles ? find_segment(a.segs, a.n_segs, t0) : 0;
+  for (int64_t t = t0; t < t1; t += kU) {
+    uint4 q[kU][kLoads];
+    const T* gp[kU];
+    int64_t base[kU], nel[kU];
+    bool full[kU];
+#pragma unroll
+    for (int k = 0; k < kU; ++k) {
+      const int64_t tile = t + k;
+      gp[k] = nullptr;
+      full[k] = false;
+      base[k] = 0;
+      nel[k] = 0;
+      if (tile < t1) {
+        while (si + 1 < a.n_segs && __ldg(&a.segs[si + 1].tile_begin) <= tile) ++si;
+        const mb_segment* sg = &a.segs[si];
+        gp[k] = reinterpret_cast<const T*>(__ldg(reinterpret_cast<const unsigned long long*>(&sg->g)));
+        nel[k] = __ldg(&sg->numel);
+        base[k] = (tile - __ldg(&sg->tile_begin)) * kTile;  // first element of the tile
+        full[k] = base[k] + kTile <= nel[k] && aligned(gp[k], 16);
+        if (full[k]) {
+          // load l of thread t covers elements base + (l*kThreads + t)*kEpl .. +kEpl
+#pragma unroll
+          for (int l = 0; l < kLoads; ++l)
+            q[k][l] = __ldcs(reinterpret_cast<const uint4*>(gp[k] + base[k] + (int64_t)(l * kThreads + threadIdx.x) * kEpl));
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kU; ++k) {
+      if (full[k]) {
+#pragma unroll
+        for (int l = 0; l < kLoads; ++l) stats_elems<GDT>(q[k][l], UNSCALE, prep, acc);
+      } else if (gp[k] != nullptr) {
+        for (int l = 0; l < kLoads; ++l) {
+          int64_t e = base[k] + (int64_t)(l * kThreads + threadIdx.x) * kEpl;
+          int64_t end = e + kEpl < nel[k] ? e + kEpl : nel[k];
+          for (; e < end; ++e) {
+            float y = to_f32(gp[k][e]);
+            if (UNSCALE) y = prep(y);
+            double d = (double)y;
+            acc = __fma_rn(d, d, acc);
+          }
+        }
       }
     }
   }
-  double2 r = block_sum2(acc, bad);
+  double2 r = block_sum2(acc, 0.0);
   char* ws = static_cast<char*>(a.plan.workspace);
   double2* partials = reinterpret_cast<double2*>(ws);
   unsigned int* ticket = reinterpret_cast<unsigned int*>(ws + kTicketOffset);
   __shared__ unsigned int s_last;
   if (threadIdx.x == 0) {
+    r.y = isfinite(r.x) ? 0.0 : 1.0;
     partials[blockIdx.x] = r;
     __threadfence();
     s_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
@@ -319,9 +415,9 @@ __global__ void __launch_bounds__(kThreads) k_grad_stats(StatsArgs a) {
   // Last CTA: fixed-order reduction of the partials (deterministic for a grid).
   double a0 = 0.0, b0 = 0.0;
   for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
-    double2 q = __ldcg(&partials[i]);
-    a0 += q.x;
-    b0 += q.y;
+    double2 qq = __ldcg(&partials[i]);
+    a0 += qq.x;
+    b0 += qq.y;
   }
   double2 tot = block_sum2(a0, b0);
   if (threadIdx.x == 0) {
@@ -380,11 +476,11 @@ UpdateFn pick_update(int gdt, int odt) {
   }
 }
 using StatsFn = void (*)(StatsArgs);
-StatsFn pick_stats(int gdt) {
+StatsFn pick_stats(int gdt, bool unscale) {
   switch (gdt) {
-    case MB_F32: return &k_grad_stats<MB_F32>;
-    case MB_F16: return &k_grad_stats<MB_F16>;
-    case MB_BF16: return &k_grad_stats<MB_BF16>;
+    case MB_F32: return unscale ? &k_grad_stats<MB_F32, true> : &k_grad_stats<MB_F32, false>;
+    case MB_F16: return unscale ? &k_grad_stats<MB_F16, true> : &k_grad_stats<MB_F16, false>;
+    case MB_BF16: return unscale ? &k_grad_stats<MB_BF16, true> : &k_grad_stats<MB_BF16, false>;
     default: return nullptr;
   }
 }
@@ -462,7 +558,8 @@ MB_API int mb_grad_stats(const mb_adamw_plan* p, const mb_finalize_opts* fin, mb
   int rc = check_plan(p);
   if (rc) return rc;
   if (fin && (rc = check_fin(fin))) return rc;
-  StatsFn fn = pick_stats(p->grad_dtype);
+  const bool unscale = fin ? (fin->flags & MB_FIN_LOSS_SCALE) != 0 : false;
+  StatsFn fn = pick_stats(p->grad_dtype, unscale);
   StatsArgs a;
   a.segs = p->segs;
   a.n_tiles = p->n_tiles;
@@ -470,7 +567,7 @@ MB_API int mb_grad_stats(const mb_adamw_plan* p, const mb_finalize_opts* fin, mb
   a.plan = *p;
   a.fin = fin ? *fin : mb_finalize_opts{};
   a.fuse_finalize = fin != nullptr;
-  a.unscale = fin ? (fin->flags & MB_FIN_LOSS_SCALE) != 0 : 0;
+  a.unscale = unscale;
   int grid = grid_for(reinterpret_cast<const void*>(fn), p->n_tiles);
   if (grid > kMaxStatsBlocks) grid = kMaxStatsBlocks;
   fn<<<grid, kThreads, 0, (cudaStream_t)stream>>>(a);
