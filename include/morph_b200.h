@@ -52,7 +52,8 @@ enum {
   MB_ERR_NONFINITE = 5,          /* nonfinite gradient with the finiteness gate on   */
   MB_ERR_TIMEOUT = 6,            /* a bounded wait expired                           */
   MB_ERR_INDEX = 7,              /* a row index outside the table                    */
-  MB_ERR_UNREPRESENTABLE = 8     /* FP16 export of a nonfinite value or |w| > 65504  */
+  MB_ERR_UNREPRESENTABLE = 8,    /* FP16 export of a nonfinite value or |w| > 65504  */
+  MB_ERR_TOO_LARGE = 9           /* plan larger than the fixed no-allocation scratch */
 };
 
 /* ------------------------------------------------------------- dtypes -- */
@@ -170,6 +171,17 @@ MB_API int mb_adamw_apply(const mb_adamw_plan* plan, mb_stream_t stream);
 
 /* mb_grad_stats (fused finalize) followed by mb_adamw_apply. */
 MB_API int mb_adamw_step(const mb_adamw_plan* plan, const mb_finalize_opts* fin, mb_stream_t stream);
+
+/* No counterpart in the reference. mb_adamw_step for callers that cannot
+ * allocate device memory (a host framework whose allocator already holds the
+ * whole GPU, or a binding handed fixed buffers with no allocator of its own).
+ * plan->workspace is ignored and may be NULL: the kernels use one fixed
+ * library-owned device array instead (about 129 KiB per GPU, held until exit).
+ * At most 8192 segments; larger plans return MB_ERR_TOO_LARGE and nothing runs.
+ * The first call on a device looks the array up (cudaGetSymbolAddress): make it
+ * before any stream capture. Calls share the array; calls that may overlap on
+ * the GPU race, so order them on one stream. Allocates nothing. */
+MB_API int mb_adamw_step_noalloc(const mb_adamw_plan* plan, const mb_finalize_opts* fin, mb_stream_t stream);
 
 /* --------------------------------------- single tensor, host scalars -- */
 

@@ -20,6 +20,7 @@ MB_ERR_NONFINITE = 5
 MB_ERR_TIMEOUT = 6
 MB_ERR_INDEX = 7
 MB_ERR_UNREPRESENTABLE = 8
+MB_ERR_TOO_LARGE = 9
 
 MB_F32, MB_F16, MB_BF16, MB_NONE = 0, 1, 2, 3
 
@@ -80,6 +81,7 @@ SIGNATURES = {
     "mb_step_finalize": (ctypes.c_int, [_p, _p, _p]),
     "mb_adamw_apply": (ctypes.c_int, [_p, _p]),
     "mb_adamw_step": (ctypes.c_int, [_p, _p, _p]),
+    "mb_adamw_step_noalloc": (ctypes.c_int, [_p, _p, _p]),
     "mb_adamw_update": (ctypes.c_int, [_p, _p, _p, _p, _i32, _p, _i32, _i64, _p, _p]),
     "mb_sparse_rows_update": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _p, _p, _p]),
     "mb_cast_f32": (ctypes.c_int, [_p, _p, _i32, _i64, _i32, _p, _p]),
@@ -113,7 +115,7 @@ def check(rc: int, what: str = "") -> None:
     if rc == MB_OK:
         return
     msg = status_string(rc) + (f" ({what})" if what else "")
-    if rc in (MB_ERR_ARG, MB_ERR_ALIGN, MB_ERR_UNREPRESENTABLE):
+    if rc in (MB_ERR_ARG, MB_ERR_ALIGN, MB_ERR_UNREPRESENTABLE, MB_ERR_TOO_LARGE):
         raise ValueError(msg)
     if rc in (MB_ERR_OVERFLOW_MIN_SCALE, MB_ERR_NONFINITE):
         raise FloatingPointError(msg)

@@ -525,6 +525,7 @@ MB_API const char* mb_status_string(int status) {
     case MB_ERR_TIMEOUT: return "bounded wait expired";
     case MB_ERR_INDEX: return "row index out of range";
     case MB_ERR_UNREPRESENTABLE: return "weights cannot be represented by finite FP16";
+    case MB_ERR_TOO_LARGE: return "plan exceeds the 8192-segment no-allocation scratch";
     default: return "unknown status";
   }
 }
