@@ -207,6 +207,20 @@ MB_API int mb_sparse_rows_update(float* w, float* m, float* v, int64_t rows, int
                                  int32_t grad_dtype, const mb_host_scalars* s,
                                  int32_t* err_flag, mb_stream_t stream);
 
+/* ------------------------------------------------------ Muon (kernel 4) -- */
+
+/* BF16 GEMM on the tcgen05 tensor cores: out = alpha * (a . b^T) + beta * c.
+ * a is [m, k] and b is [n, k], both row-major (K contiguous) with row pitches
+ * lda/ldb (elements, multiples of 8, 16-byte aligned bases); c and d are
+ * [m, n] BF16 with pitches ldc/ldd; dt (optional) receives out^T as [n, m]
+ * with pitch lddt; df (optional) receives out in FP32 with pitch lddf. m must
+ * be a multiple of 128, n of 256 and k of 64 (pad with zeros). A wait that
+ * exceeds its bound sets *err_flag (device int32) to 1. These are the matmuls
+ * of orthogonalize, streamtrain/optimizer.py:20-21. */
+MB_API int mb_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n, int64_t k,
+                        float alpha, float beta, const void* c, int64_t ldc, void* d, int64_t ldd, void* dt,
+                        int64_t lddt, float* df, int64_t lddf, int32_t* err_flag, mb_stream_t stream);
+
 /* FP32 -> F16/BF16 cast (round to nearest even). With check != 0 (F16 only)
  * a nonfinite value or |x| > 65504 sets *err_flag to 1 (export.py:33). */
 MB_API int mb_cast_f32(const float* src, void* dst, int32_t dst_dtype, int64_t n, int32_t check,

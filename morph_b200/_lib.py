@@ -85,6 +85,8 @@ SIGNATURES = {
     "mb_adamw_update": (ctypes.c_int, [_p, _p, _p, _p, _i32, _p, _i32, _i64, _p, _p]),
     "mb_sparse_rows_update": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _p, _p, _p]),
     "mb_cast_f32": (ctypes.c_int, [_p, _p, _i32, _i64, _i32, _p, _p]),
+    "mb_gemm_bf16": (ctypes.c_int, [_p, _i64, _p, _i64, _i64, _i64, _i64, _f, _f, _p, _i64, _p, _i64, _p, _i64,
+                                    _p, _i64, _p, _p]),
 }
 
 _LIB = None
