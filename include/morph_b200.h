@@ -209,17 +209,54 @@ MB_API int mb_sparse_rows_update(float* w, float* m, float* v, int64_t rows, int
 
 /* ------------------------------------------------------ Muon (kernel 4) -- */
 
-/* BF16 GEMM on the tcgen05 tensor cores: out = alpha * (a . b^T) + beta * c.
+/* 16-bit GEMM on the tcgen05 tensor cores: out = alpha * (a . b^T) + beta * c,
+ * FP32 accumulation. dtype (MB_BF16 or MB_F16) is the type of a, b, c, d, dt.
  * a is [m, k] and b is [n, k], both row-major (K contiguous) with row pitches
  * lda/ldb (elements, multiples of 8, 16-byte aligned bases); c and d are
- * [m, n] BF16 with pitches ldc/ldd; dt (optional) receives out^T as [n, m]
- * with pitch lddt; df (optional) receives out in FP32 with pitch lddf. m must
- * be a multiple of 128, n of 256 and k of 64 (pad with zeros). A wait that
- * exceeds its bound sets *err_flag (device int32) to 1. These are the matmuls
- * of orthogonalize, streamtrain/optimizer.py:20-21. */
-MB_API int mb_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n, int64_t k,
-                        float alpha, float beta, const void* c, int64_t ldc, void* d, int64_t ldd, void* dt,
-                        int64_t lddt, float* df, int64_t lddf, int32_t* err_flag, mb_stream_t stream);
+ * [m, n] with pitches ldc/ldd; dt (optional) receives out^T as [n, m] with
+ * pitch lddt; df (optional) receives out in FP32 with pitch lddf. m must be a
+ * multiple of 128, n of 256 and k of 64 (pad with zeros). A wait that exceeds
+ * its bound sets *err_flag (device int32) to 1. These are the matmuls of
+ * orthogonalize, streamtrain/optimizer.py:20-21. */
+MB_API int mb_gemm16(int32_t dtype, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                     int64_t k, float alpha, float beta, const void* c, int64_t ldc, void* d, int64_t ldd, void* dt,
+                     int64_t lddt, float* df, int64_t lddf, int32_t* err_flag, mb_stream_t stream);
+
+/* Muon hyperparameters of one matrix (float roundings of the reference's
+ * Python expressions, streamtrain/optimizer.py:58-61). */
+typedef struct mb_muon_args {
+  float beta_lerp;   /* momentum.lerp_(g, .05)                  */
+  float nesterov;    /* g.lerp(momentum, .95)                   */
+  float ns_a;        /* 3.4445                                  */
+  float ns_b;        /* -4.775                                  */
+  float ns_c;        /* 2.0315                                  */
+  int32_t ns_steps;  /* 5                                       */
+  float shape_scale; /* (float)(max(1, rows / cols) ** .5)      */
+  float cwd;         /* (float)(1 - lr * weight_decay)          */
+  float neg_lr;      /* (float)(-lr)                            */
+  int32_t ns_dtype;  /* Newton-Schulz operands: MB_BF16 or MB_F16 */
+} mb_muon_args;
+
+/* Device workspace for one [rows, cols] matrix (0 for invalid shapes). */
+MB_API size_t mb_muon_workspace_bytes(int64_t rows, int64_t cols);
+
+/* orthogonalize (streamtrain/optimizer.py:13-22) of an FP32 [rows, cols]
+ * matrix into out (FP32, same shape): transpose when rows > cols, divide by
+ * (Frobenius norm + 1e-7), `steps` quintic Newton-Schulz iterations with
+ * coeffs {a, b, c} on ns_dtype (MB_BF16 or MB_F16) operands with FP32
+ * accumulation; each iteration forms a I + b A + c A A in FP32 before one
+ * rounding, so the a X and (b A + c A A) X terms never cancel in 16 bits. */
+MB_API int mb_newton_schulz(const float* x, int64_t rows, int64_t cols, int32_t steps, const float* coeffs,
+                            int32_t ns_dtype, float* out, void* workspace, size_t workspace_bytes,
+                            int32_t* err_flag, mb_stream_t stream);
+
+/* One Muon step of one matrix (streamtrain/optimizer.py:55-61): momentum
+ * (FP32, updated in place) lerps toward g, the Nesterov blend is
+ * orthogonalised, scaled by shape_scale and applied with decoupled weight
+ * decay to w (FP32); out (optional) receives w in out_dtype. */
+MB_API int mb_muon_step(float* w, float* momentum, const void* g, int32_t grad_dtype, void* out, int32_t out_dtype,
+                        int64_t rows, int64_t cols, const mb_muon_args* args, void* workspace,
+                        size_t workspace_bytes, int32_t* err_flag, mb_stream_t stream);
 
 /* FP32 -> F16/BF16 cast (round to nearest even). With check != 0 (F16 only)
  * a nonfinite value or |x| > 65504 sets *err_flag to 1 (export.py:33). */

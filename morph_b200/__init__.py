@@ -12,5 +12,6 @@ importing a class that needs it raises ImportError when the library is missing.
 """
 from .precision import DynamicLossScale, fp8_eligible
 from .optim import AdamW
+from .muon import HybridMuonAdamW, orthogonalize, partition
 
-__all__ = ["AdamW", "DynamicLossScale", "fp8_eligible"]
+__all__ = ["AdamW", "DynamicLossScale", "HybridMuonAdamW", "fp8_eligible", "orthogonalize", "partition"]

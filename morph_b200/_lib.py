@@ -63,6 +63,11 @@ class Plan(ctypes.Structure):
                 ("grad_dtype", _i32), ("out_dtype", _i32)]
 
 
+class MuonArgs(ctypes.Structure):
+    _fields_ = [("beta_lerp", _f), ("nesterov", _f), ("ns_a", _f), ("ns_b", _f), ("ns_c", _f),
+                ("ns_steps", _i32), ("shape_scale", _f), ("cwd", _f), ("neg_lr", _f), ("ns_dtype", _i32)]
+
+
 class HostScalars(ctypes.Structure):
     _fields_ = [(n, _f) for n in ("cwd", "omb1", "beta2", "omb2", "bc2s", "eps", "nss", "scale", "coef")]
 
@@ -85,8 +90,11 @@ SIGNATURES = {
     "mb_adamw_update": (ctypes.c_int, [_p, _p, _p, _p, _i32, _p, _i32, _i64, _p, _p]),
     "mb_sparse_rows_update": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _p, _p, _p]),
     "mb_cast_f32": (ctypes.c_int, [_p, _p, _i32, _i64, _i32, _p, _p]),
-    "mb_gemm_bf16": (ctypes.c_int, [_p, _i64, _p, _i64, _i64, _i64, _i64, _f, _f, _p, _i64, _p, _i64, _p, _i64,
-                                    _p, _i64, _p, _p]),
+    "mb_muon_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
+    "mb_newton_schulz": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _i32, _p, _p, ctypes.c_size_t, _p, _p]),
+    "mb_muon_step": (ctypes.c_int, [_p, _p, _p, _i32, _p, _i32, _i64, _i64, _p, _p, ctypes.c_size_t, _p, _p]),
+    "mb_gemm16": (ctypes.c_int, [_i32, _p, _i64, _p, _i64, _i64, _i64, _i64, _f, _f, _p, _i64, _p, _i64, _p, _i64,
+                                 _p, _i64, _p, _p]),
 }
 
 _LIB = None

@@ -1,6 +1,7 @@
-// Kernel 4 building block: BF16 GEMM on the sm_100a tensor cores (tcgen05).
+// Kernel 4 building block: 16-bit (BF16 or FP16) GEMM on the sm_100a tensor
+// cores (tcgen05), FP32 accumulation in TMEM.
 //
-//   out = alpha * (A . B^T) + beta * C,   A [M, K], B [N, K], C/out [M, N]
+//   out = alpha * (A . B^T) + beta * C + diag * I,   A [M, K], B [N, K], C/out [M, N]
 //
 // Both operands are K-major (row-major with K contiguous), which is what
 // Newton-Schulz needs: X.X^T uses X for both; A.A uses the symmetric A for
@@ -43,20 +44,23 @@ constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + 1024 + kBarrierBytes;
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-// Instruction descriptor, kind::f16: D FP32 (bits 4-5 = 1), A and B BF16
-// (bits 7-9, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bits 17-22,
-// M >> 4 at bits 24-28.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
+// Instruction descriptor, kind::f16: D FP32 (bits 4-5 = 1), A and B of one
+// 16-bit type (bits 7-9 and 10-12: 1 = BF16, 0 = FP16), both K-major (bits 15,
+// 16 = 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+template <bool kF16>
+constexpr uint32_t idesc() {
+  return (1u << 4) | ((kF16 ? 0u : 1u) << 7) | ((kF16 ? 0u : 1u) << 10) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
 
 struct Args {
   int M, N, K;
-  float alpha, beta;
-  const __nv_bfloat16* c;
+  float alpha, beta, diag;
+  const uint16_t* c;
   int64_t ldc;
-  __nv_bfloat16* d;
+  uint16_t* d;
   int64_t ldd;
-  __nv_bfloat16* dt;
+  uint16_t* dt;
   int64_t lddt;
   float* df;
   int64_t lddf;
@@ -126,13 +130,26 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t id,
+                                        uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      "l"(adesc), "l"(bdesc), "r"(id), "r"(accumulate)
       : "memory");
+}
+
+template <bool kF16>
+__device__ __forceinline__ float h2f(uint16_t h) {
+  if constexpr (kF16) return __half2float(__ushort_as_half(h));
+  else return __uint_as_float((uint32_t)h << 16);
+}
+
+template <bool kF16>
+__device__ __forceinline__ uint16_t f2h(float x) {
+  if constexpr (kF16) return __half_as_ushort(__float2half_rn(x));
+  else return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -153,8 +170,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+template <bool kF16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args g) {
+    k_gemm16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -222,7 +240,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t a0 = smem_u32(sA + s * A_STAGE), b0 = smem_u32(sB + s * B_STAGE);
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k)
-          umma_bf16(tmem, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), (kb | k) != 0 ? 1u : 0u);
+          umma_16(tmem, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc<kF16>(), (kb | k) != 0 ? 1u : 0u);
         umma_commit(&empty[s]);
       }
       umma_commit(accum);
@@ -242,6 +260,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = g.alpha * __uint_as_float(r[j]);
         const int col = n0 + c;
+        if (g.diag != 0.0f && row >= col && row < col + 32) v[row - col] += g.diag;
         if (g.c != nullptr) {
           const uint4* src = reinterpret_cast<const uint4*>(g.c + (int64_t)row * g.ldc + col);
 #pragma unroll
@@ -250,8 +269,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
-              v[u * 8 + 2 * h] = fmaf(g.beta, __uint_as_float(ww[h] << 16), v[u * 8 + 2 * h]);
-              v[u * 8 + 2 * h + 1] = fmaf(g.beta, __uint_as_float(ww[h] & 0xffff0000u), v[u * 8 + 2 * h + 1]);
+              v[u * 8 + 2 * h] = fmaf(g.beta, h2f<kF16>((uint16_t)(ww[h] & 0xffffu)), v[u * 8 + 2 * h]);
+              v[u * 8 + 2 * h + 1] = fmaf(g.beta, h2f<kF16>((uint16_t)(ww[h] >> 16)), v[u * 8 + 2 * h + 1]);
             }
           }
         }
@@ -261,16 +280,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int u = 0; u < 4; ++u) {
             uint32_t pk[4];
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[u * 8 + 2 * h], v[u * 8 + 2 * h + 1]);
-              pk[h] = *reinterpret_cast<uint32_t*>(&b2);
-            }
+            for (int h = 0; h < 4; ++h)
+              pk[h] = (uint32_t)f2h<kF16>(v[u * 8 + 2 * h]) | ((uint32_t)f2h<kF16>(v[u * 8 + 2 * h + 1]) << 16);
             dst[u] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
         }
         if (g.dt != nullptr) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) g.dt[(int64_t)(col + j) * g.lddt + row] = __float2bfloat16_rn(v[j]);
+          for (int j = 0; j < 32; ++j) g.dt[(int64_t)(col + j) * g.lddt + row] = f2h<kF16>(v[j]);
         }
         if (g.df != nullptr) {
           float4* dst = reinterpret_cast<float4*>(g.df + (int64_t)row * g.lddf + col);
@@ -304,25 +321,27 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D BF16 row-major [rows, cols] with row pitch `ld` elements; box = 64 x box_rows, 128B swizzle.
-bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// 2-D 16-bit row-major [rows, cols] with row pitch `ld` elements; box = 64 x box_rows, 128B swizzle.
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows, bool f16) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
   cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  return fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace gemm
 
-int gemm_bf16_nt(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N, int64_t K,
-                 float alpha, float beta, const void* c, int64_t ldc, void* d, int64_t ldd, void* dt, int64_t lddt,
-                 float* df, int64_t lddf, int32_t* err, cudaStream_t stream) {
+int gemm16_nt(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N, int64_t K,
+              float alpha, float beta, float diag, const void* c, int64_t ldc, void* d, int64_t ldd, void* dt,
+              int64_t lddt, float* df, int64_t lddf, int32_t* err, cudaStream_t stream) {
   using namespace gemm;
+  if (dtype != MB_BF16 && dtype != MB_F16) return MB_ERR_ARG;
+  const bool f16 = dtype == MB_F16;
   if (!a || !b || M <= 0 || N <= 0 || K <= 0) return MB_ERR_ARG;
   if (M % BM || N % BN || K % BK || M > (1 << 30) || N > (1 << 30)) return MB_ERR_ARG;
   if (!d && !dt && !df) return MB_ERR_ARG;
@@ -333,26 +352,29 @@ int gemm_bf16_nt(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t
   if (dt && (lddt < M || !aligned(dt, 2))) return MB_ERR_ALIGN;
   if (df && (lddf < N || lddf % 4 || !aligned(df, 16))) return MB_ERR_ALIGN;
   CUtensorMap ma, mbm;
-  if (!make_map(&ma, a, M, K, lda, BM) || !make_map(&mbm, b, N, K, ldb, BN)) return MB_ERR_CUDA;
+  if (!make_map(&ma, a, M, K, lda, BM, f16) || !make_map(&mbm, b, N, K, ldb, BN, f16)) return MB_ERR_CUDA;
   static std::once_flag attr_once;
   static cudaError_t attr_rc = cudaSuccess;
   std::call_once(attr_once, [] {
-    attr_rc = cudaFuncSetAttribute(k_gemm_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_rc = cudaFuncSetAttribute(k_gemm16<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (attr_rc == cudaSuccess)
+      attr_rc = cudaFuncSetAttribute(k_gemm16<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   if (attr_rc != cudaSuccess) return MB_ERR_CUDA;
-  Args g{(int)M, (int)N, (int)K, alpha, beta, static_cast<const __nv_bfloat16*>(c), ldc,
-         static_cast<__nv_bfloat16*>(d), ldd, static_cast<__nv_bfloat16*>(dt), lddt, df, lddf, err};
+  Args g{(int)M, (int)N, (int)K, alpha, beta, diag, static_cast<const uint16_t*>(c), ldc,
+         static_cast<uint16_t*>(d), ldd, static_cast<uint16_t*>(dt), lddt, df, lddf, err};
   dim3 grid((unsigned)(N / BN), (unsigned)(M / BM));
-  k_gemm_bf16<<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
+  if (f16) k_gemm16<true><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
+  else k_gemm16<false><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
   return cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA;
 }
 
 }  // namespace mb
 
-extern "C" MB_API int mb_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
-                                   int64_t k, float alpha, float beta, const void* c, int64_t ldc, void* d,
-                                   int64_t ldd, void* dt, int64_t lddt, float* df, int64_t lddf, int32_t* err_flag,
-                                   mb_stream_t stream) {
-  return mb::gemm_bf16_nt(a, lda, b, ldb, m, n, k, alpha, beta, c, ldc, d, ldd, dt, lddt, df, lddf, err_flag,
-                          (cudaStream_t)stream);
+extern "C" MB_API int mb_gemm16(int32_t dtype, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m,
+                                int64_t n, int64_t k, float alpha, float beta, const void* c, int64_t ldc, void* d,
+                                int64_t ldd, void* dt, int64_t lddt, float* df, int64_t lddf, int32_t* err_flag,
+                                mb_stream_t stream) {
+  return mb::gemm16_nt(dtype, a, lda, b, ldb, m, n, k, alpha, beta, 0.0f, c, ldc, d, ldd, dt, lddt, df, lddf,
+                       err_flag, (cudaStream_t)stream);
 }

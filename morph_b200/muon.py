@@ -6,41 +6,224 @@ drop-in (streamtrain/optimizer.py:25-70) are built on it.
 """
 from __future__ import annotations
 
+import ctypes
+
+import numpy as np
 import torch
 
 from . import _lib
 
 
-def _check_bf16_matrix(t, name):
-    if not t.is_cuda or t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1:
-        raise ValueError(f"{name} must be a 2-D row-major BF16 CUDA tensor")
+def _check_matrix(t, name, dtype):
+    if not t.is_cuda or t.dtype != dtype or t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a 2-D row-major {dtype} CUDA tensor")
 
 
-def gemm_bf16(a, b, alpha=1.0, beta=0.0, c=None, out=True, out_t=False, out_f32=False):
-    """alpha * (a @ b.T) + beta * c on the tensor cores. a [m, k], b [n, k] BF16
-    row-major; m % 128 == 0, n % 256 == 0, k % 64 == 0. Returns (d, dt, df):
-    BF16 [m, n], BF16 [n, m] (transposed copy) and FP32 [m, n], each or None."""
-    _check_bf16_matrix(a, "a")
-    _check_bf16_matrix(b, "b")
+def gemm16(a, b, alpha=1.0, beta=0.0, c=None, out=True, out_t=False, out_f32=False):
+    """alpha * (a @ b.T) + beta * c on the tensor cores, FP32 accumulation.
+    a [m, k], b [n, k] row-major BF16 or FP16 (one type); m % 128 == 0,
+    n % 256 == 0, k % 64 == 0. Returns (d, dt, df): 16-bit [m, n], 16-bit [n, m]
+    (transposed copy) and FP32 [m, n], each or None."""
+    dtype = a.dtype
+    if dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("gemm16 operands must be bfloat16 or float16")
+    _check_matrix(a, "a", dtype)
+    _check_matrix(b, "b", dtype)
     m, k = a.shape
     n, k2 = b.shape
     if k != k2:
         raise ValueError("inner dimensions differ")
     if c is not None:
-        _check_bf16_matrix(c, "c")
+        _check_matrix(c, "c", dtype)
         if c.shape != (m, n):
             raise ValueError("c must be [m, n]")
     dev = a.device
-    d = torch.empty(m, n, dtype=torch.bfloat16, device=dev) if out else None
-    dt = torch.empty(n, m, dtype=torch.bfloat16, device=dev) if out_t else None
+    d = torch.empty(m, n, dtype=dtype, device=dev) if out else None
+    dt = torch.empty(n, m, dtype=dtype, device=dev) if out_t else None
     df = torch.empty(m, n, dtype=torch.float32, device=dev) if out_f32 else None
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     P = lambda t: None if t is None else _lib.ptr(t)  # noqa: E731
     with torch.cuda.device(dev):
-        _lib.check(_lib.lib().mb_gemm_bf16(
-            _lib.ptr(a), a.stride(0), _lib.ptr(b), b.stride(0), m, n, k, float(alpha), float(beta),
-            P(c), c.stride(0) if c is not None else 0, P(d), n, P(dt), m, P(df), n, _lib.ptr(err),
-            _lib.stream_handle()), "gemm_bf16")
+        _lib.check(_lib.lib().mb_gemm16(
+            _lib.dtype_code(dtype), _lib.ptr(a), a.stride(0), _lib.ptr(b), b.stride(0), m, n, k, float(alpha),
+            float(beta), P(c), c.stride(0) if c is not None else 0, P(d), n, P(dt), m, P(df), n, _lib.ptr(err),
+            _lib.stream_handle()), "gemm16")
     if int(err.item()):
-        raise RuntimeError("gemm_bf16: a bounded wait expired on the device")
+        raise RuntimeError("gemm16: a bounded wait expired on the device")
     return d, dt, df
+
+
+# ------------------------------------------------------------------ Muon ----
+
+NS_COEFFS = (3.4445, -4.775, 2.0315)
+# Below this smaller dimension, BF16 Newton-Schulz operands exceed the 1e-2
+# relative Frobenius tolerance on random inputs (measured, including by an exact
+# CPU emulation of BF16 rounding); FP16 operands on the same tensor-core path
+# keep the error near 2e-3 at every size.
+BF16_MIN_DIM = 256
+
+
+def ns_operand_dtype(rows, cols, ns_dtype="auto"):
+    """Operand type of Newton-Schulz: 'bf16', 'fp16', or 'auto' (BF16 when the
+    smaller dimension is at least 256, else FP16)."""
+    if ns_dtype in ("bf16", torch.bfloat16):
+        return _lib.MB_BF16
+    if ns_dtype in ("fp16", torch.float16):
+        return _lib.MB_F16
+    if ns_dtype != "auto":
+        raise ValueError("ns_dtype must be 'auto', 'bf16' or 'fp16'")
+    return _lib.MB_BF16 if min(rows, cols) >= BF16_MIN_DIM else _lib.MB_F16
+
+
+class _Workspace:
+    """Grow-only device workspace for one matrix at a time, per device."""
+
+    def __init__(self):
+        self.buf = {}
+
+    def get(self, device, nbytes):
+        t = self.buf.get(device)
+        if t is None or t.numel() < nbytes:
+            t = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+            self.buf[device] = t
+        return t
+
+
+_WS = _Workspace()
+
+
+def _workspace_for(device, rows, cols):
+    nbytes = _lib.lib().mb_muon_workspace_bytes(rows, cols)
+    if nbytes == 0:
+        raise ValueError(f"unsupported matrix shape {(rows, cols)}")
+    return _WS.get(device, nbytes), nbytes
+
+
+def orthogonalize(gradient: torch.Tensor, steps: int = 5, ns_dtype="auto") -> torch.Tensor:
+    """streamtrain/optimizer.py:13-22 on the GPU: FP32 in, FP32 out, Newton-Schulz
+    on 16-bit tensor-core GEMMs with FP32 accumulation (see ns_operand_dtype)."""
+    if gradient.dim() != 2 or not gradient.is_cuda:
+        raise ValueError("orthogonalize expects a 2-D CUDA tensor")
+    x = gradient.float().contiguous()
+    rows, cols = x.shape
+    out = torch.empty_like(x)
+    ws, nbytes = _workspace_for(x.device, rows, cols)
+    err = torch.zeros(1, dtype=torch.int32, device=x.device)
+    coeffs = torch.tensor(NS_COEFFS, dtype=torch.float32)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().mb_newton_schulz(
+            _lib.ptr(x), rows, cols, int(steps), coeffs.numpy().ctypes.data, ns_operand_dtype(rows, cols, ns_dtype),
+            _lib.ptr(out), _lib.ptr(ws), nbytes,
+            _lib.ptr(err), _lib.stream_handle()), "newton_schulz")
+    if int(err.item()):
+        raise RuntimeError("newton_schulz: a bounded wait expired on the device")
+    return out
+
+
+def partition(model):
+    """streamtrain/optimizer.py:25-31: weights of nn.Linear modules not named
+    'lm_head' go to Muon, every other parameter to AdamW."""
+    hidden = {id(module.weight) for name, module in model.named_modules()
+              if isinstance(module, torch.nn.Linear) and name != 'lm_head'}
+    muon, adam = [], []
+    for param in model.parameters():
+        (muon if id(param) in hidden else adam).append(param)
+    return muon, adam
+
+
+class HybridMuonAdamW:
+    """Drop-in for streamtrain/optimizer.py:34-70 on the B200 kernels.
+
+    Same constructor, attributes (muon, adam, momentum, lr, weight_decay),
+    zero_grad, step and state_dict/load_state_dict format. ``step`` first checks
+    every gradient for finiteness on the device (kernel 2 with the gate) and
+    raises FloatingPointError without touching any state if one is not finite;
+    then each Muon matrix takes one fused Muon step (kernel 4) and the AdamW
+    group one fused AdamW step (kernels 2 + 1)."""
+
+    def __init__(self, model, lr=1e-3, muon_lr=None, weight_decay=.01, low_precision=None, ns_dtype="auto"):
+        from .optim import AdamW
+        self.muon, adam = partition(model)
+        self.lr = lr if muon_lr is None else muon_lr
+        self.weight_decay = weight_decay
+        self.momentum = {}
+        self.low_precision = low_precision
+        self.low_precision_copies = {}
+        self.ns_dtype = ns_dtype
+        self.adam = AdamW(adam, lr=lr, weight_decay=weight_decay, betas=(.9, .95), foreach=False,
+                          low_precision=low_precision)
+        self._gate_engines = {}
+
+    def zero_grad(self, set_to_none=True):
+        for p in self.muon:
+            p.grad = None if set_to_none else torch.zeros_like(p)
+        self.adam.zero_grad(set_to_none=set_to_none)
+
+    def _check_finite(self, params):
+        """Device finiteness gate over every gradient (optimizer.py:50-51)."""
+        from .optim import StepEngine
+        grads = [(p, p.grad) for p in params if p.grad is not None]
+        if not grads:
+            return
+        by_dtype = {}
+        for p, g in grads:
+            by_dtype.setdefault(g.dtype, []).append((p, g.contiguous()))
+        for dtype, items in by_dtype.items():
+            dev = items[0][1].device
+            eng = self._gate_engines.get((dev, dtype))
+            if eng is None:
+                eng = self._gate_engines[(dev, dtype)] = StepEngine(dev)
+            for p, _ in items:
+                eng.slot(p, 0)
+            entries = [(g, g, g, g, None, 0) for _, g in items]
+            plan = eng.prepare(entries, [(0.0, 0.9, 0.9, 1e-8, 0.0, "torch")], _lib.dtype_code(dtype), _lib.MB_NONE,
+                               keys=[p for p, _ in items])
+            fin = eng.finalize_opts(_lib.MB_FIN_GATE, None)
+            with torch.cuda.device(dev):
+                _lib.check(eng.lib.mb_grad_stats(ctypes.byref(plan), ctypes.byref(fin), _lib.stream_handle()))
+            if eng.read_state().status:
+                raise FloatingPointError('nonfinite gradient; optimizer not updated')
+
+    @torch.no_grad()
+    def step(self):
+        all_params = self.muon + [p for g in self.adam.param_groups for p in g['params']]
+        self._check_finite(all_params)
+        for i, p in enumerate(self.muon):
+            if p.grad is None:
+                continue
+            if i not in self.momentum:
+                self.momentum[i] = torch.zeros_like(p)
+            self._muon_step(p, self.momentum[i], p.grad)
+        self.adam.step()
+
+    def _muon_step(self, p, momentum, grad):
+        if p.dim() != 2 or not p.is_cuda or p.dtype != torch.float32 or not p.is_contiguous():
+            raise ValueError("Muon parameters must be contiguous 2-D float32 CUDA tensors")
+        g = grad.contiguous()
+        rows, cols = p.shape
+        ws, nbytes = _workspace_for(p.device, rows, cols)
+        f = lambda x: float(np.float32(x))  # noqa: E731
+        args = _lib.MuonArgs(f(.05), f(.95), f(NS_COEFFS[0]), f(NS_COEFFS[1]), f(NS_COEFFS[2]), 5,
+                             f(max(1, p.shape[0] / p.shape[1]) ** .5), f(1 - self.lr * self.weight_decay),
+                             f(-self.lr), ns_operand_dtype(rows, cols, self.ns_dtype))
+        out, odt = None, _lib.MB_NONE
+        if self.low_precision is not None:
+            out = self.low_precision_copies.get(p)
+            if out is None:
+                out = torch.empty_like(p, dtype=self.low_precision)
+                self.low_precision_copies[p] = out
+            odt = _lib.dtype_code(self.low_precision)
+        err = torch.zeros(1, dtype=torch.int32, device=p.device)
+        with torch.cuda.device(p.device):
+            _lib.check(_lib.lib().mb_muon_step(
+                _lib.ptr(p), _lib.ptr(momentum), _lib.ptr(g), _lib.dtype_code(g.dtype),
+                None if out is None else _lib.ptr(out), odt, rows, cols, ctypes.byref(args), _lib.ptr(ws), nbytes,
+                _lib.ptr(err), _lib.stream_handle()), "muon_step")
+
+    def state_dict(self):
+        return dict(momentum=self.momentum, adam=self.adam.state_dict(), lr=self.lr, weight_decay=self.weight_decay)
+
+    def load_state_dict(self, state):
+        self.momentum = {i: value.to(self.muon[i].device) for i, value in state['momentum'].items()}
+        self.adam.load_state_dict(state['adam'])
+        self.lr, self.weight_decay = state['lr'], state['weight_decay']

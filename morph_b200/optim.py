@@ -162,23 +162,26 @@ class StepEngine:
         return _lib.StepState.from_buffer_copy(self.state_buf.cpu().numpy().tobytes())
 
     # -- launch -------------------------------------------------------------------------
-    def prepare(self, entries, groups, grad_dtype, out_dtype) -> _lib.Plan:
+    def prepare(self, entries, groups, grad_dtype, out_dtype, keys=None) -> _lib.Plan:
         """Build (or reuse) the device segment table and return the launch plan.
 
         entries: list of (p, m, v, g, out_or_None, group_index) where p, m, v are
         FP32 and may be any contiguous ranges (whole tensors or shard pieces);
-        groups: list of (lr, beta1, beta2, eps, weight_decay, table_kind)."""
+        groups: list of (lr, beta1, beta2, eps, weight_decay, table_kind);
+        keys: objects whose clock slots the segments use (default: each p)."""
         n = len(entries)
+        keys = [e[0] for e in entries] if keys is None else keys
+        slots = [self.slots[id(k)] for k in keys]
         key = tuple((p.data_ptr(), m.data_ptr(), v.data_ptr(), g.data_ptr(),
-                     0 if o is None else o.data_ptr(), p.numel(), self.slots[id(p)], gi)
-                    for p, m, v, g, o, gi in entries)
+                     0 if o is None else o.data_ptr(), g.numel(), sl, gi)
+                    for (p, m, v, g, o, gi), sl in zip(entries, slots))
         if key != self._seg_key:
             segs = np.zeros(n, _SEG_DTYPE)
             tiles = 0
-            for i, (p, m, v, g, o, gi) in enumerate(entries):
+            for i, ((p, m, v, g, o, gi), sl) in enumerate(zip(entries, slots)):
                 segs[i] = (p.data_ptr(), m.data_ptr(), v.data_ptr(), g.data_ptr(),
-                           0 if o is None else o.data_ptr(), p.numel(), tiles, self.slots[id(p)], gi)
-                tiles += (p.numel() + TILE - 1) // TILE
+                           0 if o is None else o.data_ptr(), g.numel(), tiles, sl, gi)
+                tiles += (g.numel() + TILE - 1) // TILE
             self._segs_dev = _to_device_bytes(segs, self.device)
             self._n_tiles = tiles
             self._seg_key = key
