@@ -337,6 +337,122 @@ def run_morph(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+def ns_flops(rows, cols, steps=5):
+    """Algorithmic FLOPs of orthogonalize on [rows, cols] (m <= n after the
+    transpose): per iteration X X^T (2 m^2 n), A A (2 m^3), B X (2 m^2 n)."""
+    m, n = min(rows, cols), max(rows, cols)
+    return steps * (4 * m * m * n + 2 * m ** 3)
+
+
+def run_ns_only(args):
+    """Profiling case: orthogonalize one [rows, cols] matrix (BF16 operands)
+    ``steps`` times after ``warmup`` runs; prints its time and TFLOP/s."""
+    from morph_b200 import orthogonalize
+    rows, cols = (int(x) for x in args.ns_shape.split("x"))
+    device = torch.device("cuda", 0)
+    g = torch.randn(rows, cols, device=device, generator=torch.Generator(device=device).manual_seed(0))
+    for _ in range(args.warmup):
+        orthogonalize(g, ns_dtype="bf16")
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        orthogonalize(g, ns_dtype="bf16")
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    print(json.dumps({"workload": f"orthogonalize {rows}x{cols} bf16", "ms": ms,
+                      "tflops": ns_flops(rows, cols) / (ms / 1e3) / 1e12}), flush=True)
+
+
+def run_config4(args):
+    """Config 4: hybrid Muon + AdamW at the 7B shape, one GPU. Muon: 32 layers x
+    {3 x [4096, 11008], 4 x [4096, 4096]} FP32 masters and momentum, BF16 grads
+    N(0, 1e-4), Newton-Schulz 5 iterations on BF16 tcgen05 GEMMs. AdamW: a
+    [65536, 4096] embedding and 64 vectors [4096]. Prints one JSON line with the
+    step time and the Newton-Schulz tensor throughput per matrix shape."""
+    import ctypes
+    from morph_b200 import HybridMuonAdamW, _lib
+    from morph_b200.muon import _workspace_for, NS_COEFFS
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+
+    class Model(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            layers = []
+            for _ in range(32):
+                layers += [torch.nn.Linear(11008, 4096, bias=False, device=device) for _ in range(3)]
+                layers += [torch.nn.Linear(4096, 4096, bias=False, device=device) for _ in range(4)]
+            self.layers = torch.nn.ModuleList(layers)
+            self.embedding = torch.nn.Embedding(65536, 4096, device=device)
+            self.norms = torch.nn.ParameterList([torch.nn.Parameter(torch.ones(4096, device=device))
+                                                 for _ in range(64)])
+
+    with torch.no_grad():
+        model = Model()
+    gen = torch.Generator(device=device).manual_seed(4)
+    for p in model.parameters():
+        p.grad_dtype = None
+        p.grad = (torch.randn(p.shape, device=device, generator=gen) * 1e-4).to(torch.bfloat16)
+    opt = HybridMuonAdamW(model, lr=3e-4, weight_decay=.1, ns_dtype="bf16")
+    muon_params = sum(p.numel() for p in opt.muon)
+    adam_params = sum(p.numel() for g in opt.adam.param_groups for p in g["params"])
+    for _ in range(args.warmup):
+        opt.step()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        start.record()
+        for _ in range(args.steps):
+            opt.step()
+        stop.record()
+        torch.cuda.synchronize()
+    step_ms = start.elapsed_time(stop) / args.steps
+    # per-matrix Muon step (momentum + normalise + 5 NS iterations + update), timed alone
+    per_shape = {}
+    for shape in ((4096, 11008), (4096, 4096)):
+        idx = next(i for i, q in enumerate(opt.muon) if tuple(q.shape) == shape)
+        p = opt.muon[idx]
+        rows, cols = p.shape
+        mom = opt.momentum[idx]
+        ws, nbytes = _workspace_for(device, rows, cols)
+        err = torch.zeros(1, dtype=torch.int32, device=device)
+        a = _lib.MuonArgs(.05, .95, *NS_COEFFS, 5, max(1, rows / cols) ** .5, 1 - 3e-4 * .1, -3e-4, _lib.MB_BF16)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        for i in range(3 + 10):
+            if i == 3:
+                evs[0].record()
+            _lib.check(_lib.lib().mb_muon_step(_lib.ptr(p), _lib.ptr(mom), _lib.ptr(p.grad), _lib.MB_BF16, None,
+                                               _lib.MB_NONE, rows, cols, ctypes.byref(a), _lib.ptr(ws), nbytes,
+                                               _lib.ptr(err), _lib.stream_handle()))
+        evs[1].record()
+        torch.cuda.synchronize()
+        ms = evs[0].elapsed_time(evs[1]) / 10
+        fl = ns_flops(rows, cols)
+        per_shape[f"{rows}x{cols}"] = {"ms": ms, "ns_tflops": fl / (ms / 1e3) / 1e12, "ns_flop": fl}
+    total_flop = sum(ns_flops(*q.shape) for q in opt.muon)
+    peaks = {}
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    achieved = total_flop / (step_ms / 1e3) / 1e12
+    line = {"metric": "Hybrid Muon+AdamW step (config 4, 7B shape)", "value": step_ms / 1e3, "unit": "s/step",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": False, "dtype": "bf16 NS operands, f32 state", "data": "synthetic",
+            "config": {"workload": "config4: Muon 32 x {3 x [4096,11008], 4 x [4096,4096]} + AdamW "
+                                   "[65536,4096] + 64 x [4096]", "muon_params": muon_params,
+                       "adam_params": adam_params, "ns_flop_per_step": total_flop},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "peak_kind": "measured sustained" if peaks else "fallback", "unit": "TFLOP/s",
+                         "frac": achieved / peak, "basis": "whole step time, NS FLOPs only"},
+            "per_matrix": per_shape, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def run_e2e(args, device, shapes, sizes, w, m, v, g, out):
     from morph_b200 import AdamW
     params, off = [], 0
@@ -393,6 +509,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=42, help="profiling only: fewer layers than config 2")
     ap.add_argument("--no-embedding", action="store_true", help="profiling only: drop the embedding")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 4],
+                    help="2 (default): the dense AdamW step; 4: the hybrid Muon+AdamW step")
+    ap.add_argument("--ns-shape", default=None, help="profiling only, with --config 4: one matrix, e.g. 4096x4096")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "morph":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -401,6 +520,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.config == 4:
+        run_ns_only(args) if args.ns_shape else run_config4(args)
         return
     if world > 1:
         import datetime

@@ -120,3 +120,23 @@ def test_hybrid_state_dict_format(cuda):
     opt2 = HybridMuonAdamW(model, lr=.5)
     opt2.load_state_dict(sd)
     assert opt2.lr == .01 and torch.equal(opt2.momentum[0], opt.momentum[0])
+
+
+@pytest.mark.parametrize("shape", [(4096, 11008), (4096, 4096)])
+def test_orthogonalize_full_size_bf16_vs_torch_fp32(cuda, shape):
+    """Config 4's shapes with BF16 operands against a plain PyTorch FP32
+    restatement of optimizer.py:13-22 on the GPU (TF32 off)."""
+    from morph_b200 import orthogonalize
+    g = torch.randn(shape, device=cuda, generator=torch.Generator(device=cuda).manual_seed(1))
+    out = orthogonalize(g, ns_dtype="bf16")
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        x = g / (g.norm() + 1e-7)
+        for _ in range(5):
+            a = x @ x.T
+            x = 3.4445 * x + (-4.775 * a + 2.0315 * (a @ a)) @ x
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    err = float((out - x).norm() / x.norm())
+    assert err < 1e-2, err
