@@ -40,6 +40,10 @@ METRIC = "AdamW step params/s & HBM GB/s (% of ~8 TB/s) at 4.2B params, 1/2/4/8 
 LR, BETAS, EPS, WD, MAX_NORM = 3e-4, (0.9, 0.95), 1e-8, 0.1, 1.0
 APPLY_BYTES = 28   # kernel 1: g 2 R + w,m,v 12 R + w,m,v 12 W + BF16 copy 2 W
 STATS_BYTES = 2    # kernel 2: g 2 R
+# Kernel 1's DRAM traffic per parameter, dram__bytes_read.sum + dram__bytes_write.sum
+# from one ncu capture of a one-layer launch (1.321411 GB + 1.263679 GB over
+# 94,384,128 params); traffic grows in proportion to the parameters processed.
+APPLY_TRAFFIC_PER_PARAM = (1.321411e9 + 1.263679e9) / 94384128
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -321,7 +325,9 @@ def run_morph(args, rank, world, local_rank):
         "kernels_ms": {"grad_stats": stats_ms, "adamw_apply": apply_ms, "all_gather": gather_ms},
         "roofline": {"bound": "hbm", "kernel": "mb_adamw_apply", "achieved": achieved, "peak": hbm,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
-                     "algorithmic_bytes_per_launch": APPLY_BYTES * n_local, "traffic": None},
+                     "algorithmic_bytes_per_launch": APPLY_BYTES * n_local,
+                     "traffic": APPLY_TRAFFIC_PER_PARAM * n_local,
+                     "traffic_basis": "ncu one-layer capture scaled by params per launch"},
         "gpu_launches": 2 * args.steps if world == 1 else 3 * args.steps,
         "clocks": clocks,
     }
