@@ -459,6 +459,107 @@ def run_config4(args):
     print(json.dumps(line), flush=True)
 
 
+def host_link_gbs(device, nbytes=1 << 30):
+    """Measured pinned-host <-> device copy bandwidth (H2D, D2H, both at once), GB/s."""
+    host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    host2 = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    dev2 = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    s1, s2 = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    out = {}
+    for name in ("h2d", "d2h", "both"):
+        best = 0.0
+        for _ in range(3):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            if name in ("h2d", "both"):
+                with torch.cuda.stream(s1):
+                    dev.copy_(host, non_blocking=True)
+            if name in ("d2h", "both"):
+                with torch.cuda.stream(s2):
+                    host2.copy_(dev2, non_blocking=True)
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+            best = max(best, (2 if name == "both" else 1) * nbytes / dt / 1e9)
+        out[name] = best
+    return out
+
+
+def reference_rows_cpu_time(rows_k, cols, steps=2):
+    """DiskState.update's arithmetic (streamtrain/disk.py:210-215) on the gathered
+    [k, cols] rows in RAM, the reference's CPU work for one config-5 step."""
+    import math
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(rows_k, cols, generator=g) * .02
+    m = torch.zeros_like(w)
+    v = torch.zeros_like(w)
+    grad = (torch.randn(rows_k, cols, generator=g) * 1e-3).half()
+    times = []
+    for step in range(1, steps + 2):
+        t0 = time.perf_counter()
+        gg = grad.float() * 1.0
+        m.lerp_(gg, .1)
+        v.mul_(.999).addcmul_(gg, gg, value=.001)
+        d = v.sqrt().div_(math.sqrt(1 - .999 ** step)).add_(1e-8)
+        w.mul_(1 - 1e-4 * .01).addcdiv_(m, d, value=-1e-4 / (1 - .9 ** step))
+        if step > 1:
+            times.append(time.perf_counter() - t0)
+    return times, threads
+
+
+def run_config5(args):
+    """Config 5: lazy row-sparse AdamW with the [262144, 3072] table's w, m, v in
+    pinned host memory, 10% of rows (sorted unique int64) touched per step with
+    FP16 grads N(0, 1e-3), DiskState.update hyperparameters (lr 1e-4, clip 1.0),
+    256 MiB ping-pong windows. Metric: touched params/s; roofline: host link."""
+    from morph_b200.offload import OffloadedRowTable
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    rows, cols, k = 262144, 3072, 26214
+    gen = torch.Generator().manual_seed(1234)
+    init = torch.empty(rows, cols)
+    init.normal_(0.0, 0.02, generator=gen)
+    table = OffloadedRowTable(rows, cols, init=init, device=device)
+    del init
+    steps = args.warmup + args.steps
+    idxs, grads = [], []
+    gdev = torch.Generator(device=device).manual_seed(99)
+    for step in range(steps):
+        gi = torch.Generator().manual_seed(1234 + step)
+        idxs.append(torch.randperm(rows, generator=gi)[:k].sort().values.to(device))
+        grads.append((torch.randn(k, cols, device=device, generator=gdev) * 1e-3).half())
+    for step in range(args.warmup):
+        table.step(idxs[step], grads[step], step + 1, 1e-4, 1.0)
+    table.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        start.record()
+        for step in range(args.warmup, steps):
+            table.step(idxs[step], grads[step], step + 1, 1e-4, 1.0)
+        stop.record()
+        table.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    link_bytes = 24 * k * cols
+    link = host_link_gbs(device)
+    achieved = link_bytes / (ms / 1e3) / 1e9
+    ref_times, threads = reference_rows_cpu_time(k, cols)
+    line = {"metric": "lazy row-sparse AdamW on pinned-host state (config 5)", "value": k * cols / (ms / 1e3),
+            "unit": "touched params/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "dtype": "f32 state, f16 grads", "data": "synthetic",
+            "config": {"workload": "config5: [262144,3072] table, 26214 rows/step, 256 MiB windows",
+                       "window_rows": table.window_rows, "touched_params": k * cols},
+            "roofline": {"bound": "host link", "achieved": achieved, "peak": link["both"],
+                         "unit": "GB/s", "frac": achieved / link["both"],
+                         "algorithmic_link_bytes_per_step": link_bytes, "link_measured": link},
+            "cpu_baseline": {"value": k * cols / (sum(ref_times) / len(ref_times)), "unit": "touched params/s",
+                             "cores": threads, "kind": "reference",
+                             "sample": "disk.py:210-215 arithmetic on the gathered [26214, 3072] rows in RAM"},
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def run_e2e(args, device, shapes, sizes, w, m, v, g, out):
     from morph_b200 import AdamW
     params, off = [], 0
@@ -515,8 +616,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=42, help="profiling only: fewer layers than config 2")
     ap.add_argument("--no-embedding", action="store_true", help="profiling only: drop the embedding")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 4],
-                    help="2 (default): the dense AdamW step; 4: the hybrid Muon+AdamW step")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 4, 5],
+                    help="2 (default): the dense AdamW step; 4: the hybrid Muon+AdamW step; "
+                         "5: row-sparse AdamW on pinned-host state")
     ap.add_argument("--ns-shape", default=None, help="profiling only, with --config 4: one matrix, e.g. 4096x4096")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "morph":
@@ -529,6 +631,9 @@ def main():
         return
     if args.config == 4:
         run_ns_only(args) if args.ns_shape else run_config4(args)
+        return
+    if args.config == 5:
+        run_config5(args)
         return
     if world > 1:
         import datetime

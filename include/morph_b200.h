@@ -258,6 +258,22 @@ MB_API int mb_muon_step(float* w, float* momentum, const void* g, int32_t grad_d
                         int64_t rows, int64_t cols, const mb_muon_args* args, void* workspace,
                         size_t workspace_bytes, int32_t* err_flag, mb_stream_t stream);
 
+/* Kernel 5: one row-sparse DiskState.update step on state held in pinned host
+ * memory (streamtrain/engine.py:60-163 ping-pong slots, applied to
+ * streamtrain/sparse_disk.py:122-138). host_w/m/v are [rows, cols] FP32 planes
+ * allocated pinned and mapped (cudaHostAlloc); idx (device, k sorted unique
+ * int64) and grads (device, [k, cols]) name the touched rows. The rows move
+ * through two device windows of window_rows rows ([3][window_rows][cols] FP32
+ * each): gathers on stream h2d, kernel-1 updates on stream compute, scatters
+ * on stream d2h, ordered by events; on return the work is enqueued and the
+ * compute stream is ordered after the last scatter. An out-of-range index is
+ * skipped and sets *err_flag. Calls on one device must come from one thread,
+ * in order (the events are shared per device). */
+MB_API int mb_offload_rows_step(float* host_w, float* host_m, float* host_v, int64_t rows, int64_t cols,
+                                const int64_t* idx, int64_t k, const void* grads, int32_t grad_dtype,
+                                const mb_host_scalars* s, float* window0, float* window1, int64_t window_rows,
+                                mb_stream_t compute, mb_stream_t h2d, mb_stream_t d2h, int32_t* err_flag);
+
 /* FP32 -> F16/BF16 cast (round to nearest even). With check != 0 (F16 only)
  * a nonfinite value or |x| > 65504 sets *err_flag to 1 (export.py:33). */
 MB_API int mb_cast_f32(const float* src, void* dst, int32_t dst_dtype, int64_t n, int32_t check,
