@@ -303,11 +303,16 @@ def run_morph(args, rank, world, local_rank):
     clocks = clk.summary()
     del views, entries, plan
 
-    # e2e through the public API: AdamW.step() on the model's tensors, gradients
-    # copied from pinned host memory each step, the step record read back.
+    # e2e through the public API: AdamW.step() (1 GPU) or ZeroAdamW.step()
+    # (N GPUs) on the model's tensors, gradients copied from pinned host memory
+    # each step, the step record read back.
     e2e = None
     if not args.no_e2e and world == 1:
         e2e = run_e2e(args, device, shapes, sizes, w[:total], m[:total], v[:total], g[:total], out[:total])
+    elif not args.no_e2e:
+        del w, m, v, g, full16, out
+        torch.cuda.empty_cache()
+        e2e = run_e2e_zero(args, device, shapes, sizes, rank, world)
 
     hbm, peak_kind = measured_peaks()
     achieved = APPLY_BYTES * n_local / (apply_ms / 1e3) / 1e9
@@ -558,6 +563,59 @@ def run_config5(args):
                              "sample": "disk.py:210-215 arithmetic on the gathered [26214, 3072] rows in RAM"},
             "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
+
+
+def run_e2e_zero(args, device, shapes, sizes, rank, world):
+    """e2e at N GPUs through morph_b200.zero.ZeroAdamW: each step every rank
+    copies its shard of the BF16 gradients from pinned host memory, steps (two
+    kernels, the record all-reduce, the BF16 all-gather) and reads the step
+    record back. Max over ranks."""
+    import torch.distributed as dist
+    from morph_b200.zero import ZeroAdamW
+    total = sum(sizes)
+    full = torch.empty(total, dtype=torch.float32, device=device)
+    gen = torch.Generator(device=device).manual_seed(77)
+    for s in range(0, total, 1 << 28):
+        full[s:min(total, s + (1 << 28))].normal_(0.0, 0.02, generator=gen)
+    params, off = [], 0
+    for (_, shape), n in zip(shapes, sizes):
+        params.append(full[off:off + n].view(shape))
+        off += n
+    opt = ZeroAdamW(params, LR, BETAS, EPS, WD, max_norm=MAX_NORM, gate=False, device=device)
+    del params, full
+    torch.cuda.empty_cache()
+    gflat = torch.zeros(total, dtype=torch.bfloat16, device=device)
+    grads, off = [], 0
+    for (_, shape), n in zip(shapes, sizes):
+        grads.append(gflat[off:off + n].view(shape))
+        off += n
+    lo, hi = opt.lo, opt.hi
+    host = torch.empty(hi - lo, dtype=torch.bfloat16, pin_memory=True)
+    host.normal_(0.0, 1e-4)
+    rec = torch.empty(2, dtype=torch.float64, pin_memory=True)
+    steps = max(1, min(args.steps, 5))
+
+    def step():
+        gflat[lo:hi].copy_(host, non_blocking=True)
+        opt.step(grads)
+        rec.copy_(opt.backend.record(), non_blocking=True)
+
+    for _ in range(2):
+        step()
+    dist.barrier(device_ids=[device.index])
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    stop.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(stop) / steps], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"value": total / (ms / 1e3), "unit": "params/s", "ms_per_step": ms, "steps": steps,
+            "h2d_bytes_per_step": (hi - lo) * 2 * world, "d2h_bytes_per_step": 16 * world,
+            "path": f"morph_b200.zero.ZeroAdamW.step() on {world} GPUs, grad shards H2D from pinned host"}
 
 
 def run_e2e(args, device, shapes, sizes, w, m, v, g, out):
