@@ -63,7 +63,8 @@ struct ApplyArgs {
   const mb_group* groups;
   const float2* seg_scal;  // per-segment {nss, bc2s} from the finalize
   const mb_step_state* state;
-  int64_t n_tiles;
+  int64_t tile_lo;         // first tile of the launch
+  int64_t n_tiles;         // one past the last tile of the launch
   int32_t n_segs;
 };
 
@@ -170,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, MB_APPLY_MIN_BLOCKS) k_adamw_apply(A
   mb_segment seg;
   StepScalars s;
   bool vec = false;
-  for (int64_t tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
+  for (int64_t tile = a.tile_lo + blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
     int si = cur < 0 ? find_segment(a.segs, a.n_segs, tile) : cur;
     while (si + 1 < a.n_segs && __ldg(&a.segs[si + 1].tile_begin) <= tile) ++si;
     if (si != cur) {
@@ -583,9 +584,11 @@ MB_API int mb_step_finalize(const mb_adamw_plan* p, const mb_finalize_opts* fin,
   return launch_status();
 }
 
-MB_API int mb_adamw_apply(const mb_adamw_plan* p, mb_stream_t stream) {
+MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* p, int64_t tile_lo, int64_t tile_hi, mb_stream_t stream) {
   int rc = check_plan(p);
   if (rc) return rc;
+  if (tile_lo < 0 || tile_hi > p->n_tiles || tile_lo > tile_hi) return MB_ERR_ARG;
+  if (tile_lo == tile_hi) return MB_OK;
   ApplyFn fn = pick_apply(p->grad_dtype, p->out_dtype);
   if (!fn) return MB_ERR_ARG;
   ApplyArgs a;
@@ -593,11 +596,17 @@ MB_API int mb_adamw_apply(const mb_adamw_plan* p, mb_stream_t stream) {
   a.groups = p->groups;
   a.seg_scal = reinterpret_cast<const float2*>(static_cast<const char*>(p->workspace) + kSegScalOffset);
   a.state = p->state;
-  a.n_tiles = p->n_tiles;
+  a.tile_lo = tile_lo;
+  a.n_tiles = tile_hi;
   a.n_segs = p->n_segs;
-  int grid = grid_for(reinterpret_cast<const void*>(fn), p->n_tiles);
+  int grid = grid_for(reinterpret_cast<const void*>(fn), tile_hi - tile_lo);
   fn<<<grid, kThreads, 0, (cudaStream_t)stream>>>(a);
   return launch_status();
+}
+
+MB_API int mb_adamw_apply(const mb_adamw_plan* p, mb_stream_t stream) {
+  if (!p) return MB_ERR_ARG;
+  return mb_adamw_apply_tiles(p, 0, p->n_tiles, stream);
 }
 
 MB_API int mb_adamw_step(const mb_adamw_plan* p, const mb_finalize_opts* fin, mb_stream_t stream) {

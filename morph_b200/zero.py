@@ -1,19 +1,21 @@
 """ZeRO-1 sharded AdamW across the GPUs of one node (one process per GPU).
 
 The reference is single-process; this is the one parallel strategy the B200
-build adds. The flat parameter space (all tensors in order) is cut into N
-contiguous, 16-element-aligned shards. Rank r owns the FP32 master weights and
-the two moments of its shard; every rank holds the full low-precision (BF16)
-weights the model computes with. One step:
+build adds. The flat parameter space (all tensors in order) is cut into
+16-element-aligned chunks dealt round-robin: in round k, rank r owns chunk
+k*N + r. Rank r keeps the FP32 master weights and the two moments of its
+chunks; every rank holds the full low-precision (BF16) weights the model
+computes with. One step:
 
   1. kernel 2 over this rank's slice of the (already reduced) gradients
      writes the 16-byte record {sum of squares, nonfinite} (FP64);
   2. all_reduce(SUM) of that record, so every rank takes the same skip /
-     clip / loss-scale decision;
+     clip decision;
   3. the one-CTA finalize (clip coefficient, clocks, step scalars);
-  4. kernel 1 updates the shard and writes its BF16 copy into this rank's
-     slice of the full weight buffer;
-  5. all_gather_into_tensor of the BF16 shards, in place.
+  4. per round k: kernel 1 updates this rank's chunk of round k and writes its
+     BF16 copy into place; then all_gather_into_tensor of round k's N chunks
+     (one contiguous block of the flat buffer, in place) starts on NCCL's
+     stream while round k + 1 is updated.
 
 Only those two collectives exist (NCCL over NVLink on B200 nodes). The kernel
 calls go through a backend object: ``CudaZeroBackend`` (the C-ABI library) is
@@ -27,22 +29,29 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .optim import StepEngine
+from .optim import StepEngine, TILE
 
 ALIGN = 16
 
 
-def shard_bounds(total: int, world: int, rank: int, align: int = ALIGN):
-    """[lo, hi) of rank's shard and the padded shard length (same on every rank)."""
-    per = -(-total // world)
-    per = -(-per // align) * align
-    lo = min(total, rank * per)
-    hi = min(total, lo + per)
-    return lo, hi, per
+def chunk_size(total: int, world: int, rounds: int, align: int = ALIGN) -> int:
+    """Chunk length (elements) so that rounds x world chunks cover total."""
+    cs = -(-total // (world * rounds))
+    return -(-cs // align) * align
+
+
+def rank_chunks(total: int, world: int, rank: int, rounds: int, cs: int):
+    """(round, lo, hi) of the flat ranges this rank owns (possibly empty)."""
+    out = []
+    for k in range(rounds):
+        lo = min(total, (k * world + rank) * cs)
+        hi = min(total, lo + cs)
+        out.append((k, lo, hi))
+    return out
 
 
 def shard_pieces(sizes, lo, hi):
-    """(tensor index, offset in tensor, offset in shard, length) of every piece of
+    """(tensor index, offset in tensor, offset from lo, length) of every piece of
     the tensors inside [lo, hi) of the flat space."""
     pieces, off = [], 0
     for i, n in enumerate(sizes):
@@ -60,32 +69,44 @@ class CudaZeroBackend:
         self.device = torch.device(device)
         self.engine = StepEngine(self.device)
         self._plan = None
+        self._round_tiles = []
 
     def record(self) -> torch.Tensor:
         """The device record {sumsq, nonfinite} as a 2-element FP64 view."""
         return self.engine.state_buf[:16].view(torch.float64)
 
-    def prepare(self, keys, entries, lr, betas, eps, weight_decay, grad_dtype, out_dtype):
+    def prepare(self, keys, entries, rounds, lr, betas, eps, weight_decay, grad_dtype, out_dtype):
+        """entries are ordered by round; rounds[i] is entry i's round."""
         for k in keys:
             self.engine.slot(k, 0)
         groups = [(float(lr), float(betas[0]), float(betas[1]), float(eps), float(weight_decay), "torch")]
         self._plan = self.engine.prepare(entries, groups, _lib.dtype_code(grad_dtype), _lib.dtype_code(out_dtype),
                                          keys=keys)
+        nr = (max(rounds) + 1) if rounds else 0
+        tiles = [0] * (nr + 1)
+        for e, r in zip(entries, rounds):
+            tiles[r + 1] += (e[3].numel() + TILE - 1) // TILE
+        for r in range(nr):
+            tiles[r + 1] += tiles[r]
+        self._round_tiles = tiles
 
     def stats(self, fin_flags, max_norm):
-        fin = self.engine.finalize_opts(fin_flags, max_norm)
+        self._fin = self.engine.finalize_opts(fin_flags, max_norm)
         with torch.cuda.device(self.device):
             _lib.check(self.engine.lib.mb_grad_stats(ctypes.byref(self._plan), None, _lib.stream_handle()),
                        "mb_grad_stats")
-        self._fin = fin
 
-    def finalize_and_apply(self):
+    def finalize(self):
         with torch.cuda.device(self.device):
-            s = _lib.stream_handle()
-            _lib.check(self.engine.lib.mb_step_finalize(ctypes.byref(self._plan), ctypes.byref(self._fin), s),
-                       "mb_step_finalize")
-            _lib.check(self.engine.lib.mb_adamw_apply(ctypes.byref(self._plan), s), "mb_adamw_apply")
+            _lib.check(self.engine.lib.mb_step_finalize(ctypes.byref(self._plan), ctypes.byref(self._fin),
+                                                        _lib.stream_handle()), "mb_step_finalize")
         self.engine.max_clock += 1
+
+    def apply_round(self, k):
+        lo, hi = self._round_tiles[k], self._round_tiles[k + 1]
+        with torch.cuda.device(self.device):
+            _lib.check(self.engine.lib.mb_adamw_apply_tiles(ctypes.byref(self._plan), lo, hi, _lib.stream_handle()),
+                       "mb_adamw_apply_tiles")
 
     def last_step(self) -> dict:
         st = self.engine.read_state()
@@ -97,13 +118,14 @@ class ZeroAdamW:
     """ZeRO-1 AdamW (torch AdamW arithmetic, decoupled weight decay).
 
     params: the model's FP32 tensors with identical initial values on every
-    rank (only this rank's shard is copied into the masters). After each
+    rank (only this rank's chunks are copied into the masters). After each
     ``step(grads)`` the full updated weights are in ``weights`` (one
-    low-precision tensor per parameter, views of one flat buffer)."""
+    low-precision tensor per parameter, views of one flat buffer). ``rounds``
+    is the number of update/all-gather rounds that overlap (1 on one GPU)."""
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-2, *, max_norm=None,
                  clip_mode="torch", gate=False, low_precision=torch.bfloat16, process_group=None, device=None,
-                 backend=None):
+                 backend=None, rounds=8):
         params = list(params)
         if not params:
             raise ValueError("ZeroAdamW needs parameters")
@@ -119,29 +141,41 @@ class ZeroAdamW:
         self.shapes = [tuple(p.shape) for p in params]
         self.sizes = [p.numel() for p in params]
         self.total = sum(self.sizes)
-        self.lo, self.hi, self.per = shard_bounds(self.total, self.world, self.rank)
-        self.pieces = shard_pieces(self.sizes, self.lo, self.hi)
-        self.master = torch.zeros(self.per, dtype=torch.float32, device=self.device)
-        for i, t_off, s_off, n in self.pieces:
+        self.rounds = 1 if self.world == 1 else max(1, int(rounds))
+        self.cs = chunk_size(self.total, self.world, self.rounds)
+        self.chunks = rank_chunks(self.total, self.world, self.rank, self.rounds, self.cs)
+        # pieces: (tensor index, offset in tensor, offset in the masters, length, round)
+        self.pieces = []
+        for k, lo, hi in self.chunks:
+            for i, t_off, c_off, n in shard_pieces(self.sizes, lo, hi):
+                self.pieces.append((i, t_off, k * self.cs + c_off, n, k))
+        self.master = torch.zeros(self.rounds * self.cs, dtype=torch.float32, device=self.device)
+        for i, t_off, s_off, n, _ in self.pieces:
             src = params[i].detach().reshape(-1)[t_off:t_off + n]
             self.master[s_off:s_off + n].copy_(src.to(self.device, torch.float32))
         self.exp_avg = torch.zeros_like(self.master)
         self.exp_avg_sq = torch.zeros_like(self.master)
-        self.flat_weights = torch.zeros(self.per * self.world, dtype=low_precision, device=self.device)
+        self.flat_weights = torch.zeros(self.rounds * self.world * self.cs, dtype=low_precision, device=self.device)
         off = 0
         self.weights = []
         for shape, n in zip(self.shapes, self.sizes):
             self.weights.append(self.flat_weights[off:off + n].view(shape))
             off += n
-        for i, t_off, s_off, n in self.pieces:  # this rank's slice starts out as the initial weights
-            self.flat_weights[self.lo + s_off:self.lo + s_off + n].copy_(self.master[s_off:s_off + n])
-        if self.world > 1:  # every rank starts from the full initial weights
-            dist.all_gather_into_tensor(self.flat_weights, self.flat_weights[self.lo:self.lo + self.per].clone(),
-                                        group=self.group)
+        for k, lo, hi in self.chunks:  # this rank's chunks start out as the initial weights
+            if hi > lo:
+                self.flat_weights[lo:hi].copy_(self.master[k * self.cs:k * self.cs + hi - lo])
+        for k in range(self.rounds if self.world > 1 else 0):  # every rank starts from the full weights
+            self._gather(k).wait()
         self.backend = backend if backend is not None else CudaZeroBackend(self.device)
-        # one clock key per piece (stable objects)
-        self._keys = [object() for _ in self.pieces]
-        self._prepared_for = None
+        self._keys = [object() for _ in self.pieces]  # one clock slot per piece
+
+    def _own(self, k):
+        base = (k * self.world + self.rank) * self.cs
+        return self.flat_weights[base:base + self.cs]
+
+    def _gather(self, k):
+        block = self.flat_weights[k * self.world * self.cs:(k + 1) * self.world * self.cs]
+        return dist.all_gather_into_tensor(block, self._own(k), group=self.group, async_op=True)
 
     def _fin_flags(self):
         flags = _lib.MB_FIN_GATE if self.gate else 0
@@ -150,9 +184,12 @@ class ZeroAdamW:
         return flags
 
     @torch.no_grad()
-    def step(self, grads) -> None:
+    def step(self, grads, events=None) -> None:
         """One step with the full, already reduced gradients (one tensor per
-        parameter, same shapes; FP32, FP16 or BF16, one dtype)."""
+        parameter, same shapes; FP32, FP16 or BF16, one dtype). ``events``
+        (optional, 4 CUDA events) are recorded on the current stream before
+        the statistics, after the finalize, after the last update round and
+        after the last all-gather."""
         grads = list(grads)
         if len(grads) != len(self.sizes):
             raise ValueError("one gradient per parameter expected")
@@ -160,26 +197,42 @@ class ZeroAdamW:
         if any(g.dtype != gdt for g in grads):
             raise ValueError("all gradients must share a dtype")
         flat = [g.reshape(-1) for g in grads]
-        own = self.flat_weights[self.lo:self.lo + self.per]
-        entries = []
-        for i, t_off, s_off, n in self.pieces:
+        entries, rounds = [], []
+        for i, t_off, s_off, n, k in self.pieces:
             g = flat[i][t_off:t_off + n]
             if g.device != self.device or not g.is_contiguous():
                 raise ValueError("gradients must be contiguous and on the optimizer's device")
+            own = self._own(k)
+            c_off = s_off - k * self.cs
             entries.append((self.master[s_off:s_off + n], self.exp_avg[s_off:s_off + n],
-                            self.exp_avg_sq[s_off:s_off + n], g, own[s_off:s_off + n], 0))
+                            self.exp_avg_sq[s_off:s_off + n], g, own[c_off:c_off + n], 0))
+            rounds.append(k)
+        if events:
+            events[0].record()
         if entries:
-            self.backend.prepare(self._keys, entries, self.lr, self.betas, self.eps, self.weight_decay, gdt,
-                                 self.low_precision)
+            self.backend.prepare(self._keys, entries, rounds, self.lr, self.betas, self.eps, self.weight_decay,
+                                 gdt, self.low_precision)
             self.backend.stats(self._fin_flags(), self.max_norm)
         else:
             self.backend.record().zero_()
         if self.world > 1:
             dist.all_reduce(self.backend.record(), group=self.group)
         if entries:
-            self.backend.finalize_and_apply()
-        if self.world > 1:
-            dist.all_gather_into_tensor(self.flat_weights, own, group=self.group)
+            self.backend.finalize()
+        if events:
+            events[1].record()
+        works = []
+        for k in range(self.rounds):
+            if entries:
+                self.backend.apply_round(k)
+            if self.world > 1:
+                works.append(self._gather(k))
+        if events:
+            events[2].record()
+        for w in works:
+            w.wait()
+        if events:
+            events[3].record()
         if self.gate:
             info = self.backend.last_step()
             if info["status"]:
@@ -189,7 +242,7 @@ class ZeroAdamW:
         return self.backend.last_step()
 
     def state_dict(self) -> dict:
-        """This rank's shard: masters, moments, bounds and hyperparameters."""
-        return dict(rank=self.rank, world=self.world, lo=self.lo, hi=self.hi, per=self.per,
+        """This rank's chunks: masters, moments, layout and hyperparameters."""
+        return dict(rank=self.rank, world=self.world, rounds=self.rounds, chunk=self.cs, chunks=self.chunks,
                     master=self.master.cpu(), exp_avg=self.exp_avg.cpu(), exp_avg_sq=self.exp_avg_sq.cpu(),
                     lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.weight_decay)

@@ -15,7 +15,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from morph_b200.zero import ZeroAdamW, shard_bounds, shard_pieces
+from morph_b200.zero import ZeroAdamW, chunk_size, rank_chunks, shard_pieces
 
 SHAPES = [(37,), (100, 3), (64, 64), (5,), (1000,)]
 LR, BETAS, EPS, WD = 3e-4, (.9, .95), 1e-8, .1
@@ -33,8 +33,8 @@ class OracleBackend:
     def record(self):
         return self._record
 
-    def prepare(self, keys, entries, lr, betas, eps, weight_decay, grad_dtype, out_dtype):
-        self.entries, self.hyper = entries, (lr, betas, eps, weight_decay)
+    def prepare(self, keys, entries, rounds, lr, betas, eps, weight_decay, grad_dtype, out_dtype):
+        self.entries, self.rounds, self.hyper = entries, rounds, (lr, betas, eps, weight_decay)
 
     def stats(self, fin_flags, max_norm):
         from oracle import oracle as orc
@@ -44,21 +44,28 @@ class OracleBackend:
             total, bad = total + s, bad + b
         self._record[0], self._record[1] = total, bad
 
-    def finalize_and_apply(self):
+    def finalize(self):
         from oracle import oracle as orc
         total, bad = float(self._record[0]), float(self._record[1])
-        if bad:
-            self.info = dict(norm=total ** .5, skipped=True, status=5, clip_coef=1.0)
-            return
+        self.skip = bool(bad)
         norm = total ** .5
-        coef = orc.clip_coef_torch(norm, self.max_norm) if self.max_norm else np.float32(1)
+        if self.skip:
+            self.info = dict(norm=norm, skipped=True, status=5, clip_coef=1.0)
+            return
+        self.coef = orc.clip_coef_torch(norm, self.max_norm) if self.max_norm else np.float32(1)
         self.clock += 1
+        self.info = dict(norm=norm, skipped=False, status=0, clip_coef=float(self.coef))
+
+    def apply_round(self, k):
+        from oracle import oracle as orc
+        if self.skip:
+            return
         lr, betas, eps, wd = self.hyper
         sc = orc.adamw_scalars(lr, betas[0], betas[1], eps, wd, self.clock)
-        for w, m, v, g, out, _ in self.entries:
-            orc.adamw_(w.numpy(), m.numpy(), v.numpy(), orc.grad_prepare(g.float().numpy(), coef=coef), sc)
-            out.copy_(w.to(out.dtype))
-        self.info = dict(norm=norm, skipped=False, status=0, clip_coef=float(coef))
+        for (w, m, v, g, out, _), r in zip(self.entries, self.rounds):
+            if r == k:
+                orc.adamw_(w.numpy(), m.numpy(), v.numpy(), orc.grad_prepare(g.float().numpy(), coef=self.coef), sc)
+                out.copy_(w.to(out.dtype))
 
     def last_step(self):
         return self.info
@@ -71,15 +78,20 @@ def _inputs():
     return params, grads
 
 
-def _run(world, rank):
+def _run(world, rank, rounds=3):
     params, grads = _inputs()
-    opt = ZeroAdamW(params, LR, BETAS, EPS, WD, max_norm=1.0, device="cpu", backend=OracleBackend(1.0))
+    opt = ZeroAdamW(params, LR, BETAS, EPS, WD, max_norm=1.0, device="cpu", backend=OracleBackend(1.0),
+                    rounds=rounds)
     coefs = []
     for gs in grads:
         opt.step(gs)
         coefs.append(opt.last_step()["clip_coef"])
     total = sum(p.numel() for p in params)
-    return (opt.lo, opt.hi, opt.master[:opt.hi - opt.lo].clone(), opt.flat_weights[:total].clone(), coefs)
+    # this rank's masters placed at their flat positions (NaN elsewhere)
+    flat = torch.full((total,), float("nan"))
+    for k, lo, hi in opt.chunks:
+        flat[lo:hi] = opt.master[k * opt.cs:k * opt.cs + hi - lo]
+    return (flat, opt.flat_weights[:total].clone(), coefs)
 
 
 def _worker(rank, world, port, q):
@@ -98,19 +110,22 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_shard_bounds_and_pieces_cover_the_flat_space():
+def test_round_robin_chunks_cover_the_flat_space():
     sizes = [37, 300, 4096, 5, 1000]
     total = sum(sizes)
     for world in (1, 2, 3, 8):
-        covered = []
-        for r in range(world):
-            lo, hi, per = shard_bounds(total, world, r)
-            assert per % 16 == 0 and hi - lo <= per and lo % 16 == 0
-            for i, t_off, s_off, n in shard_pieces(sizes, lo, hi):
-                start = sum(sizes[:i]) + t_off
-                assert start == lo + s_off
-                covered += list(range(start, start + n))
-        assert covered == list(range(total))
+        for rounds in (1, 3, 8):
+            cs = chunk_size(total, world, rounds)
+            assert cs % 16 == 0 and rounds * world * cs >= total
+            covered = []
+            for r in range(world):
+                for k, lo, hi in rank_chunks(total, world, r, rounds, cs):
+                    assert lo == min(total, (k * world + r) * cs)
+                    for i, t_off, c_off, n in shard_pieces(sizes, lo, hi):
+                        start = sum(sizes[:i]) + t_off
+                        assert start == lo + c_off
+                        covered += list(range(start, start + n))
+            assert sorted(covered) == list(range(total))
 
 
 def test_two_gloo_ranks_equal_one_rank():
@@ -124,11 +139,13 @@ def test_two_gloo_ranks_equal_one_rank():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    lo0, hi0, m0, full0, c0 = results[0]
-    lo1, hi1, m1, full1, c1 = results[1]
-    assert lo0 == 0 and hi0 == lo1 and c0 == c1  # one clip decision on both ranks
+    flat0, full0, c0 = results[0]
+    flat1, full1, c1 = results[1]
+    assert c0 == c1  # one clip decision on both ranks
+    masters = torch.where(torch.isnan(flat0), flat1, flat0)
+    assert not torch.isnan(masters).any()  # the two ranks' chunks cover everything
     single = _run(1, 0)
-    assert single[4] == c0
-    torch.testing.assert_close(torch.cat([m0, m1]), single[2], rtol=1e-6, atol=1e-6 * LR)
+    assert single[2] == c0
+    torch.testing.assert_close(masters, single[0], rtol=1e-6, atol=1e-6 * LR)
     assert torch.equal(full0, full1)  # both ranks hold the same gathered weights
-    torch.testing.assert_close(full0.float(), single[3].float(), rtol=1e-2, atol=0)
+    torch.testing.assert_close(full0.float(), single[1].float(), rtol=1e-2, atol=0)

@@ -32,7 +32,10 @@ def _run(device):
         opt.step([g.to(device) for g in gs])
         coefs.append(opt.last_step()["clip_coef"])
     total = sum(p.numel() for p in params)
-    return (opt.lo, opt.hi, opt.master[:opt.hi - opt.lo].cpu(), opt.flat_weights[:total].cpu(), coefs)
+    flat = torch.full((total,), float("nan"))
+    for k, lo, hi in opt.chunks:
+        flat[lo:hi] = opt.master[k * opt.cs:k * opt.cs + hi - lo].cpu()
+    return (flat, opt.flat_weights[:total].cpu(), coefs)
 
 
 def _worker(rank, world, port, q):
@@ -63,9 +66,12 @@ def test_zero_two_gpus_equal_one_gpu(cuda):
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    lo0, hi0, m0, full0, c0 = results[0]
-    lo1, hi1, m1, full1, c1 = results[1]
-    assert hi0 == lo1 and c0 == c1
+    flat0, full0, c0 = results[0]
+    flat1, full1, c1 = results[1]
+    assert c0 == c1
+    masters = torch.where(torch.isnan(flat0), flat1, flat0)
+    assert not torch.isnan(masters).any()
     single = _run(cuda)
-    torch.testing.assert_close(torch.cat([m0, m1]), single[2], rtol=1e-6, atol=1e-6 * LR)
+    torch.testing.assert_close(masters, single[0], rtol=1e-6, atol=1e-6 * LR)
     assert torch.equal(full0, full1)
+    torch.testing.assert_close(full0.float(), single[1].float(), rtol=1e-2, atol=0)
