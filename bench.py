@@ -582,7 +582,8 @@ def run_morph_zero(args, rank, world, local_rank):
     for (_, shape), n in zip(shapes, sizes):
         params.append(full[off:off + n].view(shape))
         off += n
-    opt = ZeroAdamW(params, LR, BETAS, EPS, WD, max_norm=MAX_NORM, gate=True, device=device, rounds=8)
+    opt = ZeroAdamW(params, LR, BETAS, EPS, WD, max_norm=MAX_NORM, gate=True, device=device, rounds=args.rounds,
+                    reserve_sms=args.reserve_sms)
     del params, full
     torch.cuda.empty_cache()
     gflat = torch.empty(total, dtype=torch.bfloat16, device=device)
@@ -663,7 +664,7 @@ def run_morph_zero(args, rank, world, local_rank):
                                "clip 1.0, BF16 compute copy)" if total == 4165459968 else
                                f"config2 reduced: {args.layers} layers ({total:,} params)",
                    "params": total, "grad_dtype": "bf16", "parallelism": f"zero1-dp{world}",
-                   "rounds": opt.rounds,
+                   "rounds": opt.rounds, "reserve_sms": args.reserve_sms,
                    "l2": "inputs larger than L2; no flush"},
         "hbm_gbs": (APPLY_BYTES + STATS_BYTES) * total / (ms_per_step / 1e3) / 1e9,
         "phases_ms": {"stats_allreduce_finalize": stats_ms, "update_rounds": apply_ms,
@@ -742,6 +743,8 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[2, 4, 5],
                     help="2 (default): the dense AdamW step; 4: the hybrid Muon+AdamW step; "
                          "5: row-sparse AdamW on pinned-host state")
+    ap.add_argument("--rounds", type=int, default=8, help="N > 1: update/all-gather rounds per step")
+    ap.add_argument("--reserve-sms", type=int, default=24, help="N > 1: SMs left to NCCL during the update")
     ap.add_argument("--ns-shape", default=None, help="profiling only, with --config 4: one matrix, e.g. 4096x4096")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "morph":

@@ -170,10 +170,11 @@ MB_API int mb_step_finalize(const mb_adamw_plan* plan, const mb_finalize_opts* f
 MB_API int mb_adamw_apply(const mb_adamw_plan* plan, mb_stream_t stream);
 
 /* Kernel 1 on the tiles [tile_lo, tile_hi) of a finalized plan only (segment
- * s covers tiles [s.tile_begin, next tile_begin)). Lets a caller update a
- * shard in rounds and start each round's all-gather while the next round is
- * updated. */
-MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* plan, int64_t tile_lo, int64_t tile_hi, mb_stream_t stream);
+ * s covers tiles [s.tile_begin, next tile_begin)), with at most max_ctas CTAs
+ * (<= 0: one persistent wave). Lets a caller update a shard in rounds and run
+ * each round's all-gather, on SMs left free, while the next round updates. */
+MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* plan, int64_t tile_lo, int64_t tile_hi, int32_t max_ctas,
+                                mb_stream_t stream);
 
 /* mb_grad_stats (fused finalize) followed by mb_adamw_apply. */
 MB_API int mb_adamw_step(const mb_adamw_plan* plan, const mb_finalize_opts* fin, mb_stream_t stream);

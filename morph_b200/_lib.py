@@ -85,7 +85,7 @@ SIGNATURES = {
     "mb_grad_stats": (ctypes.c_int, [_p, _p, _p]),
     "mb_step_finalize": (ctypes.c_int, [_p, _p, _p]),
     "mb_adamw_apply": (ctypes.c_int, [_p, _p]),
-    "mb_adamw_apply_tiles": (ctypes.c_int, [_p, _i64, _i64, _p]),
+    "mb_adamw_apply_tiles": (ctypes.c_int, [_p, _i64, _i64, _i32, _p]),
     "mb_adamw_step": (ctypes.c_int, [_p, _p, _p]),
     "mb_adamw_step_noalloc": (ctypes.c_int, [_p, _p, _p]),
     "mb_adamw_update": (ctypes.c_int, [_p, _p, _p, _p, _i32, _p, _i32, _i64, _p, _p]),

@@ -584,7 +584,8 @@ MB_API int mb_step_finalize(const mb_adamw_plan* p, const mb_finalize_opts* fin,
   return launch_status();
 }
 
-MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* p, int64_t tile_lo, int64_t tile_hi, mb_stream_t stream) {
+MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* p, int64_t tile_lo, int64_t tile_hi, int32_t max_ctas,
+                                mb_stream_t stream) {
   int rc = check_plan(p);
   if (rc) return rc;
   if (tile_lo < 0 || tile_hi > p->n_tiles || tile_lo > tile_hi) return MB_ERR_ARG;
@@ -600,13 +601,14 @@ MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* p, int64_t tile_lo, int64_t
   a.n_tiles = tile_hi;
   a.n_segs = p->n_segs;
   int grid = grid_for(reinterpret_cast<const void*>(fn), tile_hi - tile_lo);
+  if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
   fn<<<grid, kThreads, 0, (cudaStream_t)stream>>>(a);
   return launch_status();
 }
 
 MB_API int mb_adamw_apply(const mb_adamw_plan* p, mb_stream_t stream) {
   if (!p) return MB_ERR_ARG;
-  return mb_adamw_apply_tiles(p, 0, p->n_tiles, stream);
+  return mb_adamw_apply_tiles(p, 0, p->n_tiles, 0, stream);
 }
 
 MB_API int mb_adamw_step(const mb_adamw_plan* p, const mb_finalize_opts* fin, mb_stream_t stream) {

@@ -65,11 +65,15 @@ def shard_pieces(sizes, lo, hi):
 class CudaZeroBackend:
     """Kernel calls of one ZeRO step on the rank's GPU (C-ABI library)."""
 
-    def __init__(self, device):
+    def __init__(self, device, reserve_sms=0):
         self.device = torch.device(device)
         self.engine = StepEngine(self.device)
         self._plan = None
         self._round_tiles = []
+        # CTAs of kernel 1 when some SMs are left to the concurrent all-gather
+        # (kernel 1 runs 3 CTAs per SM at full occupancy)
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.max_ctas = 3 * max(1, sms - reserve_sms) if reserve_sms > 0 else 0
 
     def record(self) -> torch.Tensor:
         """The device record {sumsq, nonfinite} as a 2-element FP64 view."""
@@ -105,8 +109,8 @@ class CudaZeroBackend:
     def apply_round(self, k):
         lo, hi = self._round_tiles[k], self._round_tiles[k + 1]
         with torch.cuda.device(self.device):
-            _lib.check(self.engine.lib.mb_adamw_apply_tiles(ctypes.byref(self._plan), lo, hi, _lib.stream_handle()),
-                       "mb_adamw_apply_tiles")
+            _lib.check(self.engine.lib.mb_adamw_apply_tiles(ctypes.byref(self._plan), lo, hi, self.max_ctas,
+                                                            _lib.stream_handle()), "mb_adamw_apply_tiles")
 
     def last_step(self) -> dict:
         st = self.engine.read_state()
@@ -121,11 +125,12 @@ class ZeroAdamW:
     rank (only this rank's chunks are copied into the masters). After each
     ``step(grads)`` the full updated weights are in ``weights`` (one
     low-precision tensor per parameter, views of one flat buffer). ``rounds``
-    is the number of update/all-gather rounds that overlap (1 on one GPU)."""
+    is the number of update/all-gather rounds that overlap (1 on one GPU);
+    ``reserve_sms`` SMs are left free of kernel 1 for NCCL's all-gather."""
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-2, *, max_norm=None,
                  clip_mode="torch", gate=False, low_precision=torch.bfloat16, process_group=None, device=None,
-                 backend=None, rounds=8):
+                 backend=None, rounds=8, reserve_sms=24):
         params = list(params)
         if not params:
             raise ValueError("ZeroAdamW needs parameters")
@@ -166,7 +171,8 @@ class ZeroAdamW:
                 self.flat_weights[lo:hi].copy_(self.master[k * self.cs:k * self.cs + hi - lo])
         for k in range(self.rounds if self.world > 1 else 0):  # every rank starts from the full weights
             self._gather(k).wait()
-        self.backend = backend if backend is not None else CudaZeroBackend(self.device)
+        self.backend = (backend if backend is not None else
+                        CudaZeroBackend(self.device, reserve_sms if self.world > 1 else 0))
         self._keys = [object() for _ in self.pieces]  # one clock slot per piece
 
     def _own(self, k):
