@@ -352,6 +352,17 @@ def ns_flops(rows, cols, steps=5):
     return steps * (4 * m * m * n + 2 * m ** 3)
 
 
+def ns_flops_executed(rows, cols, steps=5):
+    """FLOPs the kernels execute: X X^T and the M polynomial compute only the
+    128x256 tiles not entirely below the diagonal (of the 256-padded m)."""
+    m, n = min(rows, cols), max(rows, cols)
+    mp = -(-m // 256) * 256
+    np_ = -(-n // 256) * 256
+    mt, nt = mp // 128, mp // 256
+    frac = sum(min(mt, 2 * bn + 2) for bn in range(nt)) / (mt * nt)
+    return steps * (frac * 2 * mp * mp * np_ + frac * 2 * mp ** 3 + 2 * mp * mp * np_)
+
+
 def run_ns_only(args):
     """Profiling case: orthogonalize one [rows, cols] matrix (BF16 operands)
     ``steps`` times after ``warmup`` runs; prints its time and TFLOP/s."""
@@ -370,7 +381,8 @@ def run_ns_only(args):
     torch.cuda.synchronize()
     ms = start.elapsed_time(stop) / args.steps
     print(json.dumps({"workload": f"orthogonalize {rows}x{cols} bf16", "ms": ms,
-                      "tflops": ns_flops(rows, cols) / (ms / 1e3) / 1e12}), flush=True)
+                      "tflops": ns_flops(rows, cols) / (ms / 1e3) / 1e12,
+                      "tflops_executed": ns_flops_executed(rows, cols) / (ms / 1e3) / 1e12}), flush=True)
 
 
 def run_config4(args):
@@ -438,8 +450,11 @@ def run_config4(args):
         torch.cuda.synchronize()
         ms = evs[0].elapsed_time(evs[1]) / 10
         fl = ns_flops(rows, cols)
-        per_shape[f"{rows}x{cols}"] = {"ms": ms, "ns_tflops": fl / (ms / 1e3) / 1e12, "ns_flop": fl}
+        fe = ns_flops_executed(rows, cols)
+        per_shape[f"{rows}x{cols}"] = {"ms": ms, "ns_tflops": fl / (ms / 1e3) / 1e12, "ns_flop": fl,
+                                       "ns_tflops_executed": fe / (ms / 1e3) / 1e12}
     total_flop = sum(ns_flops(*q.shape) for q in opt.muon)
+    exec_flop = sum(ns_flops_executed(*q.shape) for q in opt.muon)
     peaks = {}
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
@@ -456,7 +471,10 @@ def run_config4(args):
                        "adam_params": adam_params, "ns_flop_per_step": total_flop},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "peak_kind": "measured sustained" if peaks else "fallback", "unit": "TFLOP/s",
-                         "frac": achieved / peak, "basis": "whole step time, NS FLOPs only"},
+                         "frac": achieved / peak, "basis": "whole step time, algorithmic NS FLOPs",
+                         "achieved_executed": exec_flop / (step_ms / 1e3) / 1e12,
+                         "frac_executed": exec_flop / (step_ms / 1e3) / 1e12 / peak,
+                         "note": "symmetric GEMMs skip lower tiles, so algorithmic FLOP/s can exceed the peak"},
             "per_matrix": per_shape, "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
 

@@ -9,14 +9,23 @@
 // output. Outputs: BF16 row-major `d`, BF16 transposed `dt` (dt[j][i]) and/or
 // FP32 row-major `df`.
 //
-// One CTA computes one 128 x 256 output tile with 6 warps:
-//   warp 0   TMA producer: 4-stage ring of 128x64 (A) and 256x64 (B) BF16 tiles,
-//            128-byte swizzled, completion tracked by mbarrier transaction bytes;
-//   warp 1   owns the 256-column TMEM accumulator; one lane issues
-//            tcgen05.mma (M=128, N=256, K=16, FP32 accumulate) per 16-wide K
-//            slice and tcgen05.commit to release each stage;
+// Persistent CTAs (one per SM) walk the 128 x 256 output tiles with 6 warps:
+//   warp 0   TMA producer: 4-stage ring of 128x64 (A) and 256x64 (B) 16-bit
+//            tiles, 128-byte swizzled, completion tracked by mbarrier
+//            transaction bytes; the ring runs on across tiles;
+//   warp 1   owns two 256-column TMEM accumulators (512 columns); one lane
+//            issues tcgen05.mma (M=128, N=256, K=16, FP32 accumulate) per
+//            16-wide K slice, tcgen05.commit releases each stage and, after a
+//            tile's last slice, hands the accumulator to the epilogue;
 //   warps 2-5 epilogue: tcgen05.ld 32 lanes x 32 columns at a time, scale, add
-//            beta*C, convert, store.
+//            beta*C and diag*I, convert, store; then return the accumulator.
+// While the epilogue drains tile i from one accumulator, the MMAs of tile
+// i + 1 fill the other.
+//
+// Symmetric mode (the output is known symmetric, e.g. X X^T and polynomials
+// of it): only tiles not entirely below the diagonal are computed; elements on
+// or above the diagonal are stored directly and those strictly above are also
+// stored transposed, so every element is written exactly once.
 // Every mbarrier wait is bounded (about 2 s of %globaltimer): on expiry the CTA
 // raises the error flag, stops issuing, waits (bounded) for its own loads in
 // flight, frees its TMEM and returns.
@@ -39,22 +48,24 @@ constexpr int kWarps = 6;
 constexpr int kGemmThreads = kWarps * 32;
 constexpr int A_STAGE = BM * BK * 2;   // 16 KiB
 constexpr int B_STAGE = BN * BK * 2;   // 32 KiB
-constexpr int kBarrierBytes = 256;
+constexpr int kBarrierBytes = 256;  // full/empty rings, 2 x acc full/empty, TMEM slot, abort flag
 constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + 1024 + kBarrierBytes;
-constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 // Instruction descriptor, kind::f16: D FP32 (bits 4-5 = 1), A and B of one
 // 16-bit type (bits 7-9 and 10-12: 1 = BF16, 0 = FP16), both K-major (bits 15,
 // 16 = 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
 template <bool kF16>
-constexpr uint32_t idesc() {
+__host__ __device__ constexpr uint32_t idesc() {
   return (1u << 4) | ((kF16 ? 0u : 1u) << 7) | ((kF16 ? 0u : 1u) << 10) | ((uint32_t)(BN >> 3) << 17) |
          ((uint32_t)(BM >> 4) << 24);
 }
 
 struct Args {
   int M, N, K;
+  int n_tiles;  // tiles to compute (all, or the non-lower ones in symmetric mode)
+  int sym;      // output symmetric: see the header comment
   float alpha, beta, diag;
   const uint16_t* c;
   int64_t ldc;
@@ -170,6 +181,70 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Tile t -> (bm, bn). Plain: bm fastest (consecutive CTAs share the B tile).
+// Symmetric: column bn holds the tiles bm < min(mt, 2 bn + 2), i.e. those not
+// entirely below the diagonal (BN = 2 BM).
+__device__ __forceinline__ void tile_coords(const Args& g, int t, int& bm, int& bn) {
+  const int mt = g.M / BM;
+  if (!g.sym) {
+    bm = t % mt;
+    bn = t / mt;
+    return;
+  }
+  int c = 0;
+  for (bn = 0;; ++bn) {
+    const int h = mt < 2 * bn + 2 ? mt : 2 * bn + 2;
+    if (t < c + h) {
+      bm = t - c;
+      return;
+    }
+    c += h;
+  }
+}
+
+// Store one 32-column chunk of one row (thread's row `row`, columns col..col+31).
+template <bool kF16>
+__device__ __forceinline__ void store_chunk(const Args& g, float (&v)[32], int row, int col) {
+  const bool all_upper = row < col;            // every element strictly above the diagonal
+  const bool any_upper = row < col + 31;       // some element on/above (for direct stores: row <= col + j)
+  if (g.d != nullptr) {
+    if (!g.sym || all_upper) {
+      uint4* dst = reinterpret_cast<uint4*>(g.d + (int64_t)row * g.ldd + col);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h)
+          pk[h] = (uint32_t)f2h<kF16>(v[u * 8 + 2 * h]) | ((uint32_t)f2h<kF16>(v[u * 8 + 2 * h + 1]) << 16);
+        dst[u] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    } else if (any_upper || row == col + 31) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (row <= col + j) g.d[(int64_t)row * g.ldd + col + j] = f2h<kF16>(v[j]);
+    }
+  }
+  if (g.dt != nullptr) {
+    if (!g.sym) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) g.dt[(int64_t)(col + j) * g.lddt + row] = f2h<kF16>(v[j]);
+    } else if (any_upper) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (row < col + j) g.dt[(int64_t)(col + j) * g.lddt + row] = f2h<kF16>(v[j]);
+    }
+  }
+  if (g.df != nullptr) {
+    float4* dst = reinterpret_cast<float4*>(g.df + (int64_t)row * g.lddf + col);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) dst[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+  }
+}
+
 template <bool kF16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args g) {
@@ -179,12 +254,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sB = smem + STAGES * A_STAGE;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* acc_full = empty + STAGES;   // [2]: MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;    // [2]: epilogue -> MMA (4 arrivals: one per epilogue warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int KB = g.K / BK;
 
   if (threadIdx.x == 0) {
@@ -192,7 +267,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -209,22 +287,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t round = kb / STAGES;
-        if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag)) break;
-        mbar_expect_tx(&full[s], A_STAGE + B_STAGE);
-        tma_load_2d(sA + s * A_STAGE, &tmA, &full[s], kb * BK, m0);
-        tma_load_2d(sB + s * B_STAGE, &tmB, &full[s], kb * BK, n0);
-        issued = kb + 1;
+      int kit = 0;  // k-blocks issued so far (the ring runs on across tiles)
+      for (int t = blockIdx.x; t < g.n_tiles && !*abort_flag; t += gridDim.x) {
+        int bm, bn;
+        tile_coords(g, t, bm, bn);
+        for (int kb = 0; kb < KB; ++kb, ++kit) {
+          const int s = kit % STAGES;
+          const uint32_t round = kit / STAGES;
+          if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag)) break;
+          mbar_expect_tx(&full[s], A_STAGE + B_STAGE);
+          tma_load_2d(sA + s * A_STAGE, &tmA, &full[s], kb * BK, bm * BM);
+          tma_load_2d(sB + s * B_STAGE, &tmB, &full[s], kb * BK, bn * BN);
+        }
       }
       if (*abort_flag) {
         // Bounded wait for this CTA's own loads still in flight.
         const uint64_t t0 = globaltimer();
-        for (int kb = issued - STAGES > 0 ? issued - STAGES : 0; kb < issued; ++kb) {
-          const int s = kb % STAGES;
-          const uint32_t round = kb / STAGES;
+        for (int k = kit - STAGES > 0 ? kit - STAGES : 0; k < kit; ++k) {
+          const int s = k % STAGES;
+          const uint32_t round = k / STAGES;
           while (!mbar_try_wait(&full[s], round & 1) && globaltimer() - t0 < kWaitLimitNs) {
           }
         }
@@ -232,35 +313,53 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t round = kb / STAGES;
-        if (!mbar_wait(&full[s], round & 1, abort_flag)) break;
+      int kit = 0, it = 0;
+      for (int t = blockIdx.x; t < g.n_tiles && !*abort_flag; t += gridDim.x, ++it) {
+        const int a = it & 1;
+        const uint32_t use = it >> 1;
+        if (!mbar_wait(&acc_empty[a], (use & 1) ^ 1, abort_flag)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + s * A_STAGE), b0 = smem_u32(sB + s * B_STAGE);
+        const uint32_t acc = tmem + (uint32_t)(a * BN);
+        for (int kb = 0; kb < KB; ++kb, ++kit) {
+          const int s = kit % STAGES;
+          const uint32_t round = kit / STAGES;
+          if (!mbar_wait(&full[s], round & 1, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * A_STAGE), b0 = smem_u32(sB + s * B_STAGE);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)
-          umma_16(tmem, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc<kF16>(), (kb | k) != 0 ? 1u : 0u);
-        umma_commit(&empty[s]);
+          for (int k = 0; k < BK / 16; ++k)
+            umma_16(acc, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc<kF16>(), (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[a]);
       }
-      umma_commit(accum);
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may read
-    int ok = 0;
-    if (lane == 0) ok = mbar_wait(accum, 0, abort_flag) && !*abort_flag;
-    ok = __shfl_sync(0xffffffffu, ok, 0);  // warp-uniform: tcgen05.ld is .sync.aligned
-    tc_fence_after();
-    if (ok) {
-      const int row = m0 + q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < g.n_tiles; t += gridDim.x, ++it) {
+      const int a = it & 1;
+      const uint32_t use = it >> 1;
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(&acc_full[a], use & 1, abort_flag) && !*abort_flag;
+      ok = __shfl_sync(0xffffffffu, ok, 0);  // warp-uniform: tcgen05.ld is .sync.aligned
+      if (!ok) break;
+      tc_fence_after();
+      int bm, bn;
+      tile_coords(g, t, bm, bn);
+      const int row = bm * BM + q * 32 + lane;
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
+        tmem_ld32(tmem + (uint32_t)(a * BN) + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = g.alpha * __uint_as_float(r[j]);
-        const int col = n0 + c;
-        if (g.diag != 0.0f && row >= col && row < col + 32) v[row - col] += g.diag;
+        const int col = bn * BN + c;
+        if (g.diag != 0.0f && row >= col && row < col + 32) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col + j == row) v[j] += g.diag;  // compile-time index: v stays in registers
+        }
         if (g.c != nullptr) {
           const uint4* src = reinterpret_cast<const uint4*>(g.c + (int64_t)row * g.ldc + col);
 #pragma unroll
@@ -274,27 +373,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-        if (g.d != nullptr) {
-          uint4* dst = reinterpret_cast<uint4*>(g.d + (int64_t)row * g.ldd + col);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            uint32_t pk[4];
-#pragma unroll
-            for (int h = 0; h < 4; ++h)
-              pk[h] = (uint32_t)f2h<kF16>(v[u * 8 + 2 * h]) | ((uint32_t)f2h<kF16>(v[u * 8 + 2 * h + 1]) << 16);
-            dst[u] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          }
-        }
-        if (g.dt != nullptr) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) g.dt[(int64_t)(col + j) * g.lddt + row] = f2h<kF16>(v[j]);
-        }
-        if (g.df != nullptr) {
-          float4* dst = reinterpret_cast<float4*>(g.df + (int64_t)row * g.lddf + col);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) dst[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-        }
+        store_chunk<kF16>(g, v, row, col);
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
     }
   }
   tc_fence_before();
@@ -338,7 +421,7 @@ bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
 
 int gemm16_nt(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N, int64_t K,
               float alpha, float beta, float diag, const void* c, int64_t ldc, void* d, int64_t ldd, void* dt,
-              int64_t lddt, float* df, int64_t lddf, int32_t* err, cudaStream_t stream) {
+              int64_t lddt, float* df, int64_t lddf, int32_t* err, cudaStream_t stream, bool sym) {
   using namespace gemm;
   if (dtype != MB_BF16 && dtype != MB_F16) return MB_ERR_ARG;
   const bool f16 = dtype == MB_F16;
@@ -351,6 +434,8 @@ int gemm16_nt(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb,
   if (d && (ldd < N || ldd % 8 || !aligned(d, 16))) return MB_ERR_ALIGN;
   if (dt && (lddt < M || !aligned(dt, 2))) return MB_ERR_ALIGN;
   if (df && (lddf < N || lddf % 4 || !aligned(df, 16))) return MB_ERR_ALIGN;
+  // symmetric mode writes the lower triangle through dt == d (square output, no FP32 copy)
+  if (sym && (M != N || !d || dt != d || lddt != ldd || df)) return MB_ERR_ARG;
   CUtensorMap ma, mbm;
   if (!make_map(&ma, a, M, K, lda, BM, f16) || !make_map(&mbm, b, N, K, ldb, BN, f16)) return MB_ERR_CUDA;
   static std::once_flag attr_once;
@@ -361,9 +446,22 @@ int gemm16_nt(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb,
       attr_rc = cudaFuncSetAttribute(k_gemm16<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   if (attr_rc != cudaSuccess) return MB_ERR_CUDA;
-  Args g{(int)M, (int)N, (int)K, alpha, beta, diag, static_cast<const uint16_t*>(c), ldc,
+  const int mt = (int)(M / BM), nt = (int)(N / BN);
+  int tiles = mt * nt;
+  if (sym) {
+    tiles = 0;
+    for (int bn = 0; bn < nt; ++bn) tiles += mt < 2 * bn + 2 ? mt : 2 * bn + 2;
+  }
+  Args g{(int)M, (int)N, (int)K, tiles, sym ? 1 : 0, alpha, beta, diag, static_cast<const uint16_t*>(c), ldc,
          static_cast<uint16_t*>(d), ldd, static_cast<uint16_t*>(dt), lddt, df, lddf, err};
-  dim3 grid((unsigned)(N / BN), (unsigned)(M / BM));
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int grid = tiles < sms ? tiles : sms;
   if (f16) k_gemm16<true><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
   else k_gemm16<false><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
   return cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA;
@@ -376,5 +474,5 @@ extern "C" MB_API int mb_gemm16(int32_t dtype, const void* a, int64_t lda, const
                                 int64_t ldd, void* dt, int64_t lddt, float* df, int64_t lddf, int32_t* err_flag,
                                 mb_stream_t stream) {
   return mb::gemm16_nt(dtype, a, lda, b, ldb, m, n, k, alpha, beta, 0.0f, c, ldc, d, ldd, dt, lddt, df, lddf,
-                       err_flag, (cudaStream_t)stream);
+                       err_flag, (cudaStream_t)stream, false);
 }

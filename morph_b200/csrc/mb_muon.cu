@@ -29,7 +29,7 @@ namespace mb {
 
 int gemm16_nt(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N, int64_t K,
               float alpha, float beta, float diag, const void* c, int64_t ldc, void* d, int64_t ldd, void* dt,
-              int64_t lddt, float* df, int64_t lddf, int32_t* err, cudaStream_t stream);
+              int64_t lddt, float* df, int64_t lddf, int32_t* err, cudaStream_t stream, bool sym);
 
 namespace {
 
@@ -280,18 +280,18 @@ int ns_core(const MuonIn& in, int64_t rows, int64_t cols, int steps, const float
     const bool last = it == steps - 1;
     // the first iterate carries the prescale: undo it exactly in the FP32 epilogues
     const float s1 = it == 0 ? 1.0f / ps : 1.0f;
-    // A = X X^T
-    int rc = gemm16_nt(dtype, X, L.np, X, L.np, L.mp, L.mp, L.np, s1 * s1, 0.0f, 0.0f, nullptr, 0, A, L.mp, nullptr,
-                       0, nullptr, 0, err, s);
+    // A = X X^T (symmetric: upper tiles only, lower triangle by transposition)
+    int rc = gemm16_nt(dtype, X, L.np, X, L.np, L.mp, L.mp, L.np, s1 * s1, 0.0f, 0.0f, nullptr, 0, A, L.mp, A,
+                       L.mp, nullptr, 0, err, s, true);
     if (rc) return rc;
     // M = a I + b A + c A A, formed in FP32 and rounded once: the reference's
     // a X + (b A + c A A) X would add two nearly cancelling products.
-    rc = gemm16_nt(dtype, A, L.mp, A, L.mp, L.mp, L.mp, L.mp, c, b, a, A, L.mp, B, L.mp, nullptr, 0, nullptr, 0, err,
-                   s);
+    rc = gemm16_nt(dtype, A, L.mp, A, L.mp, L.mp, L.mp, L.mp, c, b, a, A, L.mp, B, L.mp, B, L.mp, nullptr, 0, err,
+                   s, true);
     if (rc) return rc;
     // X' = M X (reads X^T as the K-major operand; writes X' and X'^T, or FP32 at the end)
     rc = gemm16_nt(dtype, B, L.mp, XT, L.mp, L.mp, L.np, L.mp, s1, 0.0f, 0.0f, nullptr, 0, last ? nullptr : Xn, L.np,
-                   last ? nullptr : XTn, L.mp, last ? O : nullptr, L.np, err, s);
+                   last ? nullptr : XTn, L.mp, last ? O : nullptr, L.np, err, s, false);
     if (rc) return rc;
     void* t = X; X = Xn; Xn = t;
     t = XT; XT = XTn; XTn = t;
