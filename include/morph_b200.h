@@ -281,6 +281,17 @@ MB_API int mb_offload_rows_step(float* host_w, float* host_m, float* host_v, int
                                 const mb_host_scalars* s, float* window0, float* window1, int64_t window_rows,
                                 mb_stream_t compute, mb_stream_t h2d, mb_stream_t d2h, int32_t* err_flag);
 
+/* Block-scaled FP8 transport (streamtrain/precision.py:24-37): per 256-element
+ * block, scale = max(amax|x| / 448, 1e-30) and codes = e4m3fn(clamp(x / scale,
+ * -448, 448)) (round to nearest even); codes has n bytes, scales
+ * ceil(n / 256) floats. */
+MB_API int mb_fp8_pack(const float* src, int64_t n, uint8_t* codes, float* scales, mb_stream_t stream);
+
+/* Inverse of mb_fp8_pack: out[i] = (float(code[i]) * scale[i / 256]) rounded to
+ * out_dtype (MB_F32, MB_F16 or MB_BF16). */
+MB_API int mb_fp8_unpack(const uint8_t* codes, const float* scales, int64_t n, void* out, int32_t out_dtype,
+                         mb_stream_t stream);
+
 /* FP32 -> F16/BF16 cast (round to nearest even). With check != 0 (F16 only)
  * a nonfinite value or |x| > 65504 sets *err_flag to 1 (export.py:33). */
 MB_API int mb_cast_f32(const float* src, void* dst, int32_t dst_dtype, int64_t n, int32_t check,

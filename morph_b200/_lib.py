@@ -91,6 +91,8 @@ SIGNATURES = {
     "mb_adamw_update": (ctypes.c_int, [_p, _p, _p, _p, _i32, _p, _i32, _i64, _p, _p]),
     "mb_sparse_rows_update": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _p, _p, _p]),
     "mb_cast_f32": (ctypes.c_int, [_p, _p, _i32, _i64, _i32, _p, _p]),
+    "mb_fp8_pack": (ctypes.c_int, [_p, _i64, _p, _p, _p]),
+    "mb_fp8_unpack": (ctypes.c_int, [_p, _p, _i64, _p, _i32, _p]),
     "mb_offload_rows_step": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _p, _p, _p, _i64, _p, _p,
                                             _p, _p]),
     "mb_muon_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),

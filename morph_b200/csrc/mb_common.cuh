@@ -95,8 +95,32 @@ template <int DT> __device__ __forceinline__ void store1(void* p, int64_t e, flo
   static_cast<typename Elem<DT>::T*>(p)[e] = from_f32<DT>(x);
 }
 
-__device__ __forceinline__ float4 ld4f(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
-__device__ __forceinline__ void st4f(float* p, float4 v) { __stcs(reinterpret_cast<float4*>(p), v); }
+// Compile-time tuning knobs for the streaming state accesses of kernels 1 and 3:
+// MB_LD_MODE 0 = ld.global.cs (evict-first), 1 = ld.global.nc (read-only
+// path), 2 = plain ld; MB_ST_MODE 0 = st.global.cs, 1 = plain st.
+#ifndef MB_LD_MODE
+#define MB_LD_MODE 0
+#endif
+#ifndef MB_ST_MODE
+#define MB_ST_MODE 0
+#endif
+
+__device__ __forceinline__ float4 ld4f(const float* p) {
+#if MB_LD_MODE == 0
+  return __ldcs(reinterpret_cast<const float4*>(p));
+#elif MB_LD_MODE == 1
+  return __ldg(reinterpret_cast<const float4*>(p));
+#else
+  return *reinterpret_cast<const float4*>(p);
+#endif
+}
+__device__ __forceinline__ void st4f(float* p, float4 v) {
+#if MB_ST_MODE == 0
+  __stcs(reinterpret_cast<float4*>(p), v);
+#else
+  *reinterpret_cast<float4*>(p) = v;
+#endif
+}
 
 // ------------------------------------------------------------- arithmetic --
 

@@ -115,6 +115,42 @@ class DynamicLossScale:
                     steps_applied=int(st.steps_applied), steps_skipped=int(st.steps_skipped))
 
 
+def pack_fp8(value: torch.Tensor, block_size: int = 256):
+    """streamtrain/precision.py:24-30 on the GPU: E4M3FN codes (uint8, one per
+    element) and FP32 per-256-block scales of ``value`` (any shape, on a CUDA
+    device, converted to FP32 first)."""
+    if block_size != 256:
+        raise ValueError("the B200 kernels use 256-element blocks")
+    flat = value.detach().float().contiguous().reshape(-1)
+    if not flat.is_cuda:
+        raise ValueError("pack_fp8 expects a CUDA tensor")
+    n = flat.numel()
+    codes = torch.empty(n, dtype=torch.uint8, device=flat.device)
+    scales = torch.empty((n + 255) // 256, dtype=torch.float32, device=flat.device)
+    with torch.cuda.device(flat.device):
+        _lib.check(_lib.lib().mb_fp8_pack(_lib.ptr(flat), n, _lib.ptr(codes), _lib.ptr(scales),
+                                          _lib.stream_handle()), "fp8_pack")
+    return codes, scales
+
+
+def unpack_fp8(encoded: torch.Tensor, scales: torch.Tensor, dtype=torch.float16, block_size: int = 256):
+    """streamtrain/precision.py:33-37 on the GPU: values = code * scale, rounded
+    to ``dtype`` (float16, bfloat16 or float32), flat."""
+    if block_size != 256:
+        raise ValueError("the B200 kernels use 256-element blocks")
+    if not encoded.is_cuda or encoded.dtype != torch.uint8 or not encoded.is_contiguous():
+        raise ValueError("encoded must be contiguous uint8 on a CUDA device")
+    n = encoded.numel()
+    sc = scales.contiguous().float()
+    if sc.numel() != (n + 255) // 256:
+        raise ValueError("one scale per 256-element block expected")
+    out = torch.empty(n, dtype=dtype, device=encoded.device)
+    with torch.cuda.device(encoded.device):
+        _lib.check(_lib.lib().mb_fp8_unpack(_lib.ptr(encoded), _lib.ptr(sc), n, _lib.ptr(out),
+                                            _lib.dtype_code(dtype), _lib.stream_handle()), "fp8_unpack")
+    return out
+
+
 def fp8_eligible(name: str) -> bool:
     """streamtrain/precision.py:20-21: the SwiGLU projections may travel as FP8."""
     return any(name.endswith(suffix) for suffix in ('ffn.gate.weight', 'ffn.up.weight', 'ffn.down.weight'))

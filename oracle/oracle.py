@@ -222,6 +222,28 @@ def sparse_rows_(w, m, v, idx, grads32, scalars: Scalars):
         raise IndexError('row index out of range')
 
 
+def pack_fp8(x: np.ndarray, block_size=256):
+    """streamtrain/precision.py:24-30 restated with torch CPU ops (the float8
+    conversion is torch's): (uint8 codes, float32 per-block scales)."""
+    import torch
+    flat = torch.from_numpy(np.ascontiguousarray(x, np.float32)).reshape(-1)
+    padding = (-flat.numel()) % block_size
+    padded = torch.nn.functional.pad(flat, (0, padding)).reshape(-1, block_size)
+    scales = (padded.abs().amax(1) / 448.).clamp_min(1e-30)
+    codes = (padded / scales[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+    return codes.reshape(-1)[:flat.numel()].numpy(), scales.numpy()
+
+
+def unpack_fp8(codes: np.ndarray, scales: np.ndarray, dtype="float16", block_size=256):
+    """streamtrain/precision.py:33-37 restated with torch CPU ops."""
+    import torch
+    c = torch.from_numpy(np.ascontiguousarray(codes, np.uint8))
+    n = c.numel()
+    padded = torch.nn.functional.pad(c, (0, (-n) % block_size))
+    values = padded.view(torch.float8_e4m3fn).float().reshape(-1, block_size)
+    return (values * torch.from_numpy(scales)[:, None]).to(getattr(torch, dtype)).reshape(-1)[:n].numpy()
+
+
 # --------------------------------------------------------------------- Muon --
 
 def orthogonalize(g: np.ndarray, steps=5) -> np.ndarray:

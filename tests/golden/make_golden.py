@@ -25,6 +25,7 @@ Cases:
   clip_*  torch clip_grad_norm_ (morph/training/runner.py:100) coefficients.
   ls_*    DynamicLossScale sequences (tests/test_fp16.py:59-72 pattern and
           growth/cap/minimum-scale behaviour).
+  fp8_*   pack_fp8 / unpack_fp8 (streamtrain/precision.py:24-37) block transport.
 """
 from __future__ import annotations
 
@@ -223,6 +224,22 @@ def run_loss_scale(out):
     out['ls_events'] = np.frombuffer(b'o' + b'sssosssssoooo' + b'ssssss', np.uint8)
 
 
+def run_fp8(out):
+    """precision.py:24-37 pack_fp8 / unpack_fp8 on seeded inputs (a ragged size,
+    an all-zero block, a block with one huge value)."""
+    from streamtrain.precision import pack_fp8, unpack_fp8
+    r = orc.rng(519)
+    x = r.standard_normal(519 + 256 * 3, dtype=np.float32)
+    x[256:512] = 0.0
+    x[600] = 3.0e4
+    enc, scales = pack_fp8(torch.from_numpy(x))
+    out['fp8_in'] = x
+    out['fp8_encoded'] = enc.numpy()
+    out['fp8_scales'] = scales.numpy()
+    out['fp8_unpacked_f16'] = unpack_fp8(enc, scales, torch.float16).numpy()
+    out['fp8_unpacked_f32'] = unpack_fp8(enc, scales, torch.float32).numpy()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', default=os.environ.get('MORPH_REFERENCE', ''))
@@ -241,6 +258,7 @@ def main():
     run_muon(out)
     run_clip(out)
     run_loss_scale(out)
+    run_fp8(out)
     np.savez_compressed(args.out, **out)
     print('wrote', args.out, os.path.getsize(args.out), 'bytes,', len(out), 'arrays')
 

@@ -207,3 +207,13 @@ def test_bf16_cast_is_round_to_nearest_even():
     ref = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     np.testing.assert_array_equal(got, ref)
     np.testing.assert_array_equal(orc.bf16_to_f32(got), torch.from_numpy(x).to(torch.bfloat16).float().numpy())
+
+
+def test_oracle_fp8_matches_reference(golden):
+    codes, scales = orc.pack_fp8(golden["fp8_in"])
+    np.testing.assert_array_equal(codes, golden["fp8_encoded"])
+    np.testing.assert_array_equal(scales, golden["fp8_scales"])
+    np.testing.assert_array_equal(orc.unpack_fp8(codes, scales, "float16"), golden["fp8_unpacked_f16"])
+    x = golden["fp8_in"]
+    back = orc.unpack_fp8(codes, scales, "float32")
+    assert np.linalg.norm(back - x) / np.linalg.norm(x) < .04  # tests/test_fp16.py:16-19
