@@ -393,7 +393,7 @@ def run_config4(args):
     step time and the Newton-Schulz tensor throughput per matrix shape."""
     import ctypes
     from morph_b200 import HybridMuonAdamW, _lib
-    from morph_b200.muon import _workspace_for, NS_COEFFS
+    from morph_b200.muon import NS_COEFFS
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
 
@@ -429,30 +429,44 @@ def run_config4(args):
         stop.record()
         torch.cuda.synchronize()
     step_ms = start.elapsed_time(stop) / args.steps
-    # per-matrix Muon step (momentum + normalise + 5 NS iterations + update), timed alone
+    # Muon step of one matrix, and of the batch the optimizer launches for the
+    # shape (momentum + normalise + 5 NS iterations + update), timed alone
     per_shape = {}
     for shape in ((4096, 11008), (4096, 4096)):
-        idx = next(i for i, q in enumerate(opt.muon) if tuple(q.shape) == shape)
-        p = opt.muon[idx]
-        rows, cols = p.shape
-        mom = opt.momentum[idx]
-        ws, nbytes = _workspace_for(device, rows, cols)
+        idxs = [i for i, q in enumerate(opt.muon) if tuple(q.shape) == shape]
+        rows, cols = shape
+        per = _lib.lib().mb_muon_batch_workspace_bytes(1, rows, cols)
+        cap = max(1, min(_lib.MB_MUON_MAX_BATCH, opt.workspace_limit // per))
+        size = -(-len(idxs) // -(-len(idxs) // cap))
         err = torch.zeros(1, dtype=torch.int32, device=device)
         a = _lib.MuonArgs(.05, .95, *NS_COEFFS, 5, max(1, rows / cols) ** .5, 1 - 3e-4 * .1, -3e-4, _lib.MB_BF16)
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-        for i in range(3 + 10):
-            if i == 3:
-                evs[0].record()
-            _lib.check(_lib.lib().mb_muon_step(_lib.ptr(p), _lib.ptr(mom), _lib.ptr(p.grad), _lib.MB_BF16, None,
-                                               _lib.MB_NONE, rows, cols, ctypes.byref(a), _lib.ptr(ws), nbytes,
-                                               _lib.ptr(err), _lib.stream_handle()))
-        evs[1].record()
-        torch.cuda.synchronize()
-        ms = evs[0].elapsed_time(evs[1]) / 10
-        fl = ns_flops(rows, cols)
-        fe = ns_flops_executed(rows, cols)
-        per_shape[f"{rows}x{cols}"] = {"ms": ms, "ns_tflops": fl / (ms / 1e3) / 1e12, "ns_flop": fl,
-                                       "ns_tflops_executed": fe / (ms / 1e3) / 1e12}
+        entry = {}
+        for batch in (1, size):
+            sel = idxs[:batch]
+            nbytes = _lib.lib().mb_muon_batch_workspace_bytes(batch, rows, cols)
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            table = ctypes.c_void_p * batch
+            w_t = table(*[_lib.ptr(opt.muon[i]) for i in sel])
+            m_t = table(*[_lib.ptr(opt.momentum[i]) for i in sel])
+            g_t = table(*[_lib.ptr(opt.muon[i].grad) for i in sel])
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            reps = 10 if batch == 1 else 3
+            for i in range(3 + reps):
+                if i == 3:
+                    evs[0].record()
+                _lib.check(_lib.lib().mb_muon_step_batched(w_t, m_t, g_t, _lib.MB_BF16, None, _lib.MB_NONE, batch,
+                                                           rows, cols, ctypes.byref(a), _lib.ptr(ws), nbytes,
+                                                           _lib.ptr(err), _lib.stream_handle()))
+            evs[1].record()
+            torch.cuda.synchronize()
+            del ws
+            ms = evs[0].elapsed_time(evs[1]) / reps / batch  # per matrix
+            fl = ns_flops(rows, cols)
+            fe = ns_flops_executed(rows, cols)
+            entry["single" if batch == 1 else f"batch{batch}"] = {
+                "ms_per_matrix": ms, "ns_tflops": fl / (ms / 1e3) / 1e12, "ns_flop": fl,
+                "ns_tflops_executed": fe / (ms / 1e3) / 1e12}
+        per_shape[f"{rows}x{cols}"] = entry
     total_flop = sum(ns_flops(*q.shape) for q in opt.muon)
     exec_flop = sum(ns_flops_executed(*q.shape) for q in opt.muon)
     peaks = {}

@@ -244,8 +244,16 @@ typedef struct mb_muon_args {
   int32_t ns_dtype;  /* Newton-Schulz operands: MB_BF16 or MB_F16 */
 } mb_muon_args;
 
-/* Device workspace for one [rows, cols] matrix (0 for invalid shapes). */
+/* Most matrices one mb_muon_step_batched call takes. */
+#define MB_MUON_MAX_BATCH 64
+
+/* Device workspace for one [rows, cols] matrix, enough for mb_newton_schulz
+ * and mb_muon_step (0 for invalid shapes). */
 MB_API size_t mb_muon_workspace_bytes(int64_t rows, int64_t cols);
+
+/* Device workspace for mb_muon_step_batched over `batch` [rows, cols]
+ * matrices (0 for invalid shapes or batch outside 1..MB_MUON_MAX_BATCH). */
+MB_API size_t mb_muon_batch_workspace_bytes(int32_t batch, int64_t rows, int64_t cols);
 
 /* orthogonalize (streamtrain/optimizer.py:13-22) of an FP32 [rows, cols]
  * matrix into out (FP32, same shape): transpose when rows > cols, divide by
@@ -264,6 +272,16 @@ MB_API int mb_newton_schulz(const float* x, int64_t rows, int64_t cols, int32_t 
 MB_API int mb_muon_step(float* w, float* momentum, const void* g, int32_t grad_dtype, void* out, int32_t out_dtype,
                         int64_t rows, int64_t cols, const mb_muon_args* args, void* workspace,
                         size_t workspace_bytes, int32_t* err_flag, mb_stream_t stream);
+
+/* mb_muon_step over `batch` matrices of one shape (the per-parameter loop of
+ * streamtrain/optimizer.py:52-61, which runs the matrices one after another):
+ * w, momentum, g and out (null when out_dtype is MB_NONE) are HOST arrays of
+ * `batch` device pointers; every launch of the step covers the whole batch.
+ * Each matrix gets exactly the arithmetic of mb_muon_step. */
+MB_API int mb_muon_step_batched(float* const* w, float* const* momentum, const void* const* g, int32_t grad_dtype,
+                                void* const* out, int32_t out_dtype, int32_t batch, int64_t rows, int64_t cols,
+                                const mb_muon_args* args, void* workspace, size_t workspace_bytes,
+                                int32_t* err_flag, mb_stream_t stream);
 
 /* Kernel 5: one row-sparse DiskState.update step on state held in pinned host
  * memory (streamtrain/engine.py:60-163 ping-pong slots, applied to

@@ -23,6 +23,7 @@ MB_ERR_UNREPRESENTABLE = 8
 MB_ERR_TOO_LARGE = 9
 
 MB_F32, MB_F16, MB_BF16, MB_NONE = 0, 1, 2, 3
+MB_MUON_MAX_BATCH = 64
 
 MB_FIN_LOSS_SCALE = 1
 MB_FIN_GATE = 2
@@ -96,8 +97,11 @@ SIGNATURES = {
     "mb_offload_rows_step": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _p, _p, _p, _i64, _p, _p,
                                             _p, _p]),
     "mb_muon_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
+    "mb_muon_batch_workspace_bytes": (ctypes.c_size_t, [_i32, _i64, _i64]),
     "mb_newton_schulz": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _i32, _p, _p, ctypes.c_size_t, _p, _p]),
     "mb_muon_step": (ctypes.c_int, [_p, _p, _p, _i32, _p, _i32, _i64, _i64, _p, _p, ctypes.c_size_t, _p, _p]),
+    "mb_muon_step_batched": (ctypes.c_int, [_p, _p, _p, _i32, _p, _i32, _i32, _i64, _i64, _p, _p, ctypes.c_size_t,
+                                            _p, _p]),
     "mb_gemm16": (ctypes.c_int, [_i32, _p, _i64, _p, _i64, _i64, _i64, _i64, _f, _f, _p, _i64, _p, _i64, _p, _i64,
                                  _p, _i64, _p, _p]),
 }

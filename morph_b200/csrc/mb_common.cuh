@@ -186,6 +186,41 @@ __device__ __forceinline__ int find_segment(const mb_segment* segs, int n, int64
   return lo;
 }
 
+// Matrices one batched Muon / GEMM launch covers (pointer tables travel as
+// kernel parameters).
+constexpr int kMaxBatch = 64;
+
+// One (possibly batched) launch of kernel 4's tcgen05 GEMM:
+//   out[b] = alpha * A[b] . B[b]^T + beta * C[b] + diag * I   for b < batch,
+// A[b] at a + b*sa, etc. (element strides); see mb_gemm.cu.
+struct GemmCall {
+  int dtype;  // MB_BF16 or MB_F16 operands and 16-bit outputs
+  const void* a;
+  int64_t lda, sa;
+  const void* b;
+  int64_t ldb, sb;
+  int64_t M, N, K;
+  int batch;
+  float alpha, beta, diag;
+  const void* c;
+  int64_t ldc, sc;
+  void* d;
+  int64_t ldd, sd;
+  void* dt;
+  int64_t lddt, sdt;
+  float* df;
+  int64_t lddf, sdf;
+  bool sym;
+  float* const* upd_w;  // fused Muon update: host array of `batch` w pointers (or null)
+  void* const* upd_out; // host array of `batch` copy pointers (or null)
+  int upd_odt;
+  bool upd_tall;
+  int64_t upd_m, upd_n, upd_cols;
+  float upd_scale, upd_cwd, upd_neglr;
+  int32_t* err;
+};
+int gemm16(const GemmCall& call, cudaStream_t stream);
+
 // Number of CTAs a persistent streaming kernel launches on the current device.
 int persistent_blocks(const void* kernel, int threads, size_t smem);
 // Persistent grid for `fn` (kThreads threads), capped at n_tiles; cached per device.

@@ -64,17 +64,28 @@ __host__ __device__ constexpr uint32_t idesc() {
 
 struct Args {
   int M, N, K;
-  int n_tiles;  // tiles to compute (all, or the non-lower ones in symmetric mode)
+  int n_tiles;  // tiles per matrix (all, or the non-lower ones in symmetric mode)
+  int batch;    // matrices; tile index t covers matrix t / n_tiles
   int sym;      // output symmetric: see the header comment
   float alpha, beta, diag;
   const uint16_t* c;
-  int64_t ldc;
+  int64_t ldc, sc;  // row pitch, matrix stride (elements)
   uint16_t* d;
-  int64_t ldd;
+  int64_t ldd, sd;
   uint16_t* dt;
-  int64_t lddt;
+  int64_t lddt, sdt;
   float* df;
-  int64_t lddf;
+  int64_t lddf, sdf;
+  // Fused Muon update (upd): for each valid output element o of matrix b,
+  // w = fma(o * upd_scale, upd_neglr, w * upd_cwd) on upd_w[b] (FP32
+  // [rows, cols]); o[i][j] is w[i][j], or w[j][i] when upd_tall; upd_out[b]
+  // (optional) receives w in upd_odt. upd_vec: w rows are 16-byte aligned
+  // (cols % 4 == 0), so wide chunks move as float4.
+  int upd, upd_odt, upd_tall, upd_vec;
+  int64_t upd_m, upd_n, upd_cols;  // valid rows / columns of the output, w's row length
+  float upd_scale, upd_cwd, upd_neglr;
+  float* upd_w[kMaxBatch];
+  void* upd_out[kMaxBatch];
   int32_t* err;
 };
 
@@ -123,11 +134,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
           "r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -185,10 +196,12 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Tile t -> (bm, bn). Plain: bm fastest (consecutive CTAs share the B tile).
-// Symmetric: column bn holds the tiles bm < min(mt, 2 bn + 2), i.e. those not
-// entirely below the diagonal (BN = 2 BM).
-__device__ __forceinline__ void tile_coords(const Args& g, int t, int& bm, int& bn) {
+// Tile t -> (matrix, bm, bn). Plain: bm fastest (consecutive CTAs share the B
+// tile). Symmetric: column bn holds the tiles bm < min(mt, 2 bn + 2), i.e. those
+// not entirely below the diagonal (BN = 2 BM).
+__device__ __forceinline__ void tile_coords(const Args& g, int tb, int& mat, int& bm, int& bn) {
+  mat = tb / g.n_tiles;
+  const int t = tb - mat * g.n_tiles;
   const int mt = g.M / BM;
   if (!g.sym) {
     bm = t % mt;
@@ -206,14 +219,16 @@ __device__ __forceinline__ void tile_coords(const Args& g, int t, int& bm, int& 
   }
 }
 
-// Store one 32-column chunk of one row (thread's row `row`, columns col..col+31).
+// Store one 32-column chunk of one row (thread's row `row`, columns col..col+31)
+// of matrix `mat`.
 template <bool kF16>
-__device__ __forceinline__ void store_chunk(const Args& g, float (&v)[32], int row, int col) {
+__device__ __forceinline__ void store_chunk(const Args& g, float (&v)[32], int mat, int row, int col) {
   const bool all_upper = row < col;            // every element strictly above the diagonal
-  const bool any_upper = row < col + 31;       // some element on/above (for direct stores: row <= col + j)
+  const bool any_upper = row < col + 31;       // some element strictly above
   if (g.d != nullptr) {
+    uint16_t* d = g.d + (int64_t)mat * g.sd;
     if (!g.sym || all_upper) {
-      uint4* dst = reinterpret_cast<uint4*>(g.d + (int64_t)row * g.ldd + col);
+      uint4* dst = reinterpret_cast<uint4*>(d + (int64_t)row * g.ldd + col);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         uint32_t pk[4];
@@ -222,26 +237,63 @@ __device__ __forceinline__ void store_chunk(const Args& g, float (&v)[32], int r
           pk[h] = (uint32_t)f2h<kF16>(v[u * 8 + 2 * h]) | ((uint32_t)f2h<kF16>(v[u * 8 + 2 * h + 1]) << 16);
         dst[u] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-    } else if (any_upper || row == col + 31) {
+    } else if (row <= col + 31) {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (row <= col + j) g.d[(int64_t)row * g.ldd + col + j] = f2h<kF16>(v[j]);
+        if (row <= col + j) d[(int64_t)row * g.ldd + col + j] = f2h<kF16>(v[j]);
     }
   }
   if (g.dt != nullptr) {
+    uint16_t* dt = g.dt + (int64_t)mat * g.sdt;
     if (!g.sym) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) g.dt[(int64_t)(col + j) * g.lddt + row] = f2h<kF16>(v[j]);
+      for (int j = 0; j < 32; ++j) dt[(int64_t)(col + j) * g.lddt + row] = f2h<kF16>(v[j]);
     } else if (any_upper) {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (row < col + j) g.dt[(int64_t)(col + j) * g.lddt + row] = f2h<kF16>(v[j]);
+        if (row < col + j) dt[(int64_t)(col + j) * g.lddt + row] = f2h<kF16>(v[j]);
     }
   }
   if (g.df != nullptr) {
-    float4* dst = reinterpret_cast<float4*>(g.df + (int64_t)row * g.lddf + col);
+    float4* dst = reinterpret_cast<float4*>(g.df + (int64_t)mat * g.sdf + (int64_t)row * g.lddf + col);
 #pragma unroll
     for (int u = 0; u < 8; ++u) dst[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+  }
+  if (g.upd && row < g.upd_m) {
+    // optimizer.py:60-61: u = o * shape_scale; w = w * (1 - lr wd) + (-lr) u
+    float* w = g.upd_w[mat];
+    void* out = g.upd_out[mat];
+    if (!g.upd_tall && g.upd_vec && col + 32 <= g.upd_n) {
+      float4* wp = reinterpret_cast<float4*>(w + (int64_t)row * g.upd_cols + col);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        float4 x = wp[u];
+        float r[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h)
+          r[h] = __fmaf_rn(__fmul_rn(v[4 * u + h], g.upd_scale), g.upd_neglr, __fmul_rn(r[h], g.upd_cwd));
+        wp[u] = make_float4(r[0], r[1], r[2], r[3]);
+        if (out != nullptr) {
+          const int64_t e = (int64_t)row * g.upd_cols + col + 4 * u;
+          if (g.upd_odt == MB_BF16) store4<MB_BF16>(out, e, r);
+          else store4<MB_F16>(out, e, r);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (col + j < g.upd_n) {
+          const int64_t e =
+              g.upd_tall ? (int64_t)(col + j) * g.upd_cols + row : (int64_t)row * g.upd_cols + col + j;
+          const float wn = __fmaf_rn(__fmul_rn(v[j], g.upd_scale), g.upd_neglr, __fmul_rn(w[e], g.upd_cwd));
+          w[e] = wn;
+          if (out != nullptr) {
+            if (g.upd_odt == MB_BF16) static_cast<__nv_bfloat16*>(out)[e] = __float2bfloat16_rn(wn);
+            else static_cast<__half*>(out)[e] = __float2half_rn(wn);
+          }
+        }
+      }
+    }
   }
 }
 
@@ -288,16 +340,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       int kit = 0;  // k-blocks issued so far (the ring runs on across tiles)
-      for (int t = blockIdx.x; t < g.n_tiles && !*abort_flag; t += gridDim.x) {
-        int bm, bn;
-        tile_coords(g, t, bm, bn);
+      const int total = g.n_tiles * g.batch;
+      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+        int mat, bm, bn;
+        tile_coords(g, t, mat, bm, bn);
         for (int kb = 0; kb < KB; ++kb, ++kit) {
           const int s = kit % STAGES;
           const uint32_t round = kit / STAGES;
           if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag)) break;
           mbar_expect_tx(&full[s], A_STAGE + B_STAGE);
-          tma_load_2d(sA + s * A_STAGE, &tmA, &full[s], kb * BK, bm * BM);
-          tma_load_2d(sB + s * B_STAGE, &tmB, &full[s], kb * BK, bn * BN);
+          tma_load_3d(sA + s * A_STAGE, &tmA, &full[s], kb * BK, bm * BM, mat);
+          tma_load_3d(sB + s * B_STAGE, &tmB, &full[s], kb * BK, bn * BN, mat);
         }
       }
       if (*abort_flag) {
@@ -314,7 +367,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       int kit = 0, it = 0;
-      for (int t = blockIdx.x; t < g.n_tiles && !*abort_flag; t += gridDim.x, ++it) {
+      const int total = g.n_tiles * g.batch;
+      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++it) {
         const int a = it & 1;
         const uint32_t use = it >> 1;
         if (!mbar_wait(&acc_empty[a], (use & 1) ^ 1, abort_flag)) break;
@@ -337,7 +391,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may read
     int it = 0;
-    for (int t = blockIdx.x; t < g.n_tiles; t += gridDim.x, ++it) {
+    const int total = g.n_tiles * g.batch;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
       const int a = it & 1;
       const uint32_t use = it >> 1;
       int ok = 0;
@@ -345,8 +400,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);  // warp-uniform: tcgen05.ld is .sync.aligned
       if (!ok) break;
       tc_fence_after();
-      int bm, bn;
-      tile_coords(g, t, bm, bn);
+      int mat, bm, bn;
+      tile_coords(g, t, mat, bm, bn);
       const int row = bm * BM + q * 32 + lane;
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
@@ -361,7 +416,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (col + j == row) v[j] += g.diag;  // compile-time index: v stays in registers
         }
         if (g.c != nullptr) {
-          const uint4* src = reinterpret_cast<const uint4*>(g.c + (int64_t)row * g.ldc + col);
+          const uint4* src = reinterpret_cast<const uint4*>(g.c + (int64_t)mat * g.sc + (int64_t)row * g.ldc + col);
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             uint4 w4 = src[u];
@@ -373,7 +428,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-        store_chunk<kF16>(g, v, row, col);
+        store_chunk<kF16>(g, v, mat, row, col);
       }
       tc_fence_before();
       __syncwarp();
@@ -404,40 +459,55 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D 16-bit row-major [rows, cols] with row pitch `ld` elements; box = 64 x box_rows, 128B swizzle.
-bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows, bool f16) {
+// 3-D 16-bit tensor [batch][rows][cols], row pitch `ld` and matrix stride
+// `bstride` (elements); box = 64 x box_rows x 1, 128B swizzle.
+bool make_map(CUtensorMap* map, const void* base, int64_t batch, int64_t rows, int64_t cols, int64_t ld,
+              int64_t bstride, int box_rows, bool f16) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  return fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)((batch > 1 ? bstride : rows * ld) * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base),
+            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace gemm
 
-int gemm16_nt(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N, int64_t K,
-              float alpha, float beta, float diag, const void* c, int64_t ldc, void* d, int64_t ldd, void* dt,
-              int64_t lddt, float* df, int64_t lddf, int32_t* err, cudaStream_t stream, bool sym) {
+int gemm16(const GemmCall& q, cudaStream_t stream) {
   using namespace gemm;
-  if (dtype != MB_BF16 && dtype != MB_F16) return MB_ERR_ARG;
-  const bool f16 = dtype == MB_F16;
-  if (!a || !b || M <= 0 || N <= 0 || K <= 0) return MB_ERR_ARG;
+  if (q.dtype != MB_BF16 && q.dtype != MB_F16) return MB_ERR_ARG;
+  const bool f16 = q.dtype == MB_F16;
+  const int64_t M = q.M, N = q.N, K = q.K;
+  if (!q.a || !q.b || M <= 0 || N <= 0 || K <= 0 || q.batch <= 0) return MB_ERR_ARG;
   if (M % BM || N % BN || K % BK || M > (1 << 30) || N > (1 << 30)) return MB_ERR_ARG;
-  if (!d && !dt && !df) return MB_ERR_ARG;
-  if (lda < K || ldb < K || (lda % 8) || (ldb % 8)) return MB_ERR_ALIGN;
-  if (!aligned(a, 16) || !aligned(b, 16)) return MB_ERR_ALIGN;
-  if (c && (ldc < N || ldc % 8 || !aligned(c, 16))) return MB_ERR_ALIGN;
-  if (d && (ldd < N || ldd % 8 || !aligned(d, 16))) return MB_ERR_ALIGN;
-  if (dt && (lddt < M || !aligned(dt, 2))) return MB_ERR_ALIGN;
-  if (df && (lddf < N || lddf % 4 || !aligned(df, 16))) return MB_ERR_ALIGN;
-  // symmetric mode writes the lower triangle through dt == d (square output, no FP32 copy)
-  if (sym && (M != N || !d || dt != d || lddt != ldd || df)) return MB_ERR_ARG;
+  if (!q.d && !q.dt && !q.df && !q.upd_w) return MB_ERR_ARG;
+  if (q.batch > kMaxBatch) return MB_ERR_ARG;
+  if (q.lda < K || q.ldb < K || (q.lda % 8) || (q.ldb % 8)) return MB_ERR_ALIGN;
+  if (!aligned(q.a, 16) || !aligned(q.b, 16)) return MB_ERR_ALIGN;
+  if (q.batch > 1 && (q.sa < M * q.lda || q.sb < N * q.ldb || q.sa % 8 || q.sb % 8)) return MB_ERR_ALIGN;
+  if (q.c && (q.ldc < N || q.ldc % 8 || !aligned(q.c, 16) || q.sc % 8)) return MB_ERR_ALIGN;
+  if (q.d && (q.ldd < N || q.ldd % 8 || !aligned(q.d, 16) || q.sd % 8)) return MB_ERR_ALIGN;
+  if (q.dt && (q.lddt < M || !aligned(q.dt, 2))) return MB_ERR_ALIGN;
+  if (q.df && (q.lddf < N || q.lddf % 4 || !aligned(q.df, 16) || q.sdf % 4)) return MB_ERR_ALIGN;
+  bool upd_vec = q.upd_w != nullptr && q.upd_cols % 4 == 0;
+  if (q.upd_w) {
+    if (q.upd_m > M || q.upd_n > N || q.upd_cols <= 0) return MB_ERR_ARG;
+    if (q.upd_out && q.upd_odt != MB_BF16 && q.upd_odt != MB_F16) return MB_ERR_ARG;
+    for (int b = 0; b < q.batch; ++b) {
+      if (!q.upd_w[b] || (q.upd_out && !q.upd_out[b])) return MB_ERR_ARG;
+      upd_vec = upd_vec && aligned(q.upd_w[b], 16) && (!q.upd_out || aligned(q.upd_out[b], 8));
+    }
+  }
+  // symmetric mode writes the lower triangle through dt == d (square output, no other outputs)
+  if (q.sym && (M != N || !q.d || q.dt != q.d || q.lddt != q.ldd || q.sdt != q.sd || q.df || q.upd_w))
+    return MB_ERR_ARG;
   CUtensorMap ma, mbm;
-  if (!make_map(&ma, a, M, K, lda, BM, f16) || !make_map(&mbm, b, N, K, ldb, BN, f16)) return MB_ERR_CUDA;
+  if (!make_map(&ma, q.a, q.batch, M, K, q.lda, q.sa, BM, f16) ||
+      !make_map(&mbm, q.b, q.batch, N, K, q.ldb, q.sb, BN, f16))
+    return MB_ERR_CUDA;
   static std::once_flag attr_once;
   static cudaError_t attr_rc = cudaSuccess;
   std::call_once(attr_once, [] {
@@ -448,12 +518,29 @@ int gemm16_nt(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb,
   if (attr_rc != cudaSuccess) return MB_ERR_CUDA;
   const int mt = (int)(M / BM), nt = (int)(N / BN);
   int tiles = mt * nt;
-  if (sym) {
+  if (q.sym) {
     tiles = 0;
     for (int bn = 0; bn < nt; ++bn) tiles += mt < 2 * bn + 2 ? mt : 2 * bn + 2;
   }
-  Args g{(int)M, (int)N, (int)K, tiles, sym ? 1 : 0, alpha, beta, diag, static_cast<const uint16_t*>(c), ldc,
-         static_cast<uint16_t*>(d), ldd, static_cast<uint16_t*>(dt), lddt, df, lddf, err};
+  if ((int64_t)tiles * q.batch > (int64_t)1 << 30) return MB_ERR_ARG;
+  Args g{};
+  g.M = (int)M; g.N = (int)N; g.K = (int)K;
+  g.n_tiles = tiles; g.batch = q.batch; g.sym = q.sym ? 1 : 0;
+  g.alpha = q.alpha; g.beta = q.beta; g.diag = q.diag;
+  g.c = static_cast<const uint16_t*>(q.c); g.ldc = q.ldc; g.sc = q.sc;
+  g.d = static_cast<uint16_t*>(q.d); g.ldd = q.ldd; g.sd = q.sd;
+  g.dt = static_cast<uint16_t*>(q.dt); g.lddt = q.lddt; g.sdt = q.sdt;
+  g.df = q.df; g.lddf = q.lddf; g.sdf = q.sdf;
+  if (q.upd_w) {
+    g.upd = 1; g.upd_odt = q.upd_odt; g.upd_tall = q.upd_tall ? 1 : 0; g.upd_vec = upd_vec ? 1 : 0;
+    g.upd_m = q.upd_m; g.upd_n = q.upd_n; g.upd_cols = q.upd_cols;
+    g.upd_scale = q.upd_scale; g.upd_cwd = q.upd_cwd; g.upd_neglr = q.upd_neglr;
+    for (int b = 0; b < q.batch; ++b) {
+      g.upd_w[b] = q.upd_w[b];
+      g.upd_out[b] = q.upd_out ? q.upd_out[b] : nullptr;
+    }
+  }
+  g.err = q.err;
   static int sms = 0;
   if (sms == 0) {
     int dev = 0;
@@ -461,7 +548,8 @@ int gemm16_nt(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb,
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
   }
-  const int grid = tiles < sms ? tiles : sms;
+  const int64_t work = (int64_t)tiles * q.batch;
+  const int grid = (int)(work < sms ? work : sms);
   if (f16) k_gemm16<true><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
   else k_gemm16<false><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
   return cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA;
@@ -473,6 +561,16 @@ extern "C" MB_API int mb_gemm16(int32_t dtype, const void* a, int64_t lda, const
                                 int64_t n, int64_t k, float alpha, float beta, const void* c, int64_t ldc, void* d,
                                 int64_t ldd, void* dt, int64_t lddt, float* df, int64_t lddf, int32_t* err_flag,
                                 mb_stream_t stream) {
-  return mb::gemm16_nt(dtype, a, lda, b, ldb, m, n, k, alpha, beta, 0.0f, c, ldc, d, ldd, dt, lddt, df, lddf,
-                       err_flag, (cudaStream_t)stream, false);
+  mb::GemmCall q{};
+  q.dtype = dtype;
+  q.a = a; q.lda = lda;
+  q.b = b; q.ldb = ldb;
+  q.M = m; q.N = n; q.K = k; q.batch = 1;
+  q.alpha = alpha; q.beta = beta; q.diag = 0.0f;
+  q.c = c; q.ldc = ldc;
+  q.d = d; q.ldd = ldd;
+  q.dt = dt; q.lddt = lddt;
+  q.df = df; q.lddf = lddf;
+  q.err = err_flag;
+  return mb::gemm16(q, (cudaStream_t)stream);
 }

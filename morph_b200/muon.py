@@ -141,7 +141,8 @@ class HybridMuonAdamW:
     then each Muon matrix takes one fused Muon step (kernel 4) and the AdamW
     group one fused AdamW step (kernels 2 + 1)."""
 
-    def __init__(self, model, lr=1e-3, muon_lr=None, weight_decay=.01, low_precision=None, ns_dtype="auto"):
+    def __init__(self, model, lr=1e-3, muon_lr=None, weight_decay=.01, low_precision=None, ns_dtype="auto",
+                 workspace_limit=4 << 30):
         from .optim import AdamW
         self.muon, adam = partition(model)
         self.lr = lr if muon_lr is None else muon_lr
@@ -150,9 +151,11 @@ class HybridMuonAdamW:
         self.low_precision = low_precision
         self.low_precision_copies = {}
         self.ns_dtype = ns_dtype
+        self.workspace_limit = int(workspace_limit)
         self.adam = AdamW(adam, lr=lr, weight_decay=weight_decay, betas=(.9, .95), foreach=False,
                           low_precision=low_precision)
         self._gate_engines = {}
+        self._err = {}
 
     def zero_grad(self, set_to_none=True):
         for p in self.muon:
@@ -188,37 +191,62 @@ class HybridMuonAdamW:
     def step(self):
         all_params = self.muon + [p for g in self.adam.param_groups for p in g['params']]
         self._check_finite(all_params)
+        for dev, err in self._err.items():  # the gate above synchronised: last step's flags are final
+            if int(err.item()):
+                err.zero_()
+                raise RuntimeError("muon step: a bounded wait expired on the device")
+        # matrices of one shape and gradient dtype share every launch (kernel 4 batches them)
+        groups = {}
         for i, p in enumerate(self.muon):
             if p.grad is None:
                 continue
+            if p.dim() != 2 or not p.is_cuda or p.dtype != torch.float32 or not p.is_contiguous():
+                raise ValueError("Muon parameters must be contiguous 2-D float32 CUDA tensors")
             if i not in self.momentum:
                 self.momentum[i] = torch.zeros_like(p)
-            self._muon_step(p, self.momentum[i], p.grad)
+            g = p.grad.contiguous()
+            groups.setdefault((p.device, tuple(p.shape), g.dtype), []).append((p, self.momentum[i], g))
+        for (dev, (rows, cols), _), items in groups.items():
+            per = _lib.lib().mb_muon_batch_workspace_bytes(1, rows, cols)
+            if per == 0:
+                raise ValueError(f"unsupported matrix shape {(rows, cols)}")
+            cap = max(1, min(_lib.MB_MUON_MAX_BATCH, self.workspace_limit // per))
+            n_batches = -(-len(items) // cap)
+            size = -(-len(items) // n_batches)
+            for b in range(0, len(items), size):
+                self._muon_batch(items[b:b + size], rows, cols)
         self.adam.step()
 
-    def _muon_step(self, p, momentum, grad):
-        if p.dim() != 2 or not p.is_cuda or p.dtype != torch.float32 or not p.is_contiguous():
-            raise ValueError("Muon parameters must be contiguous 2-D float32 CUDA tensors")
-        g = grad.contiguous()
-        rows, cols = p.shape
-        ws, nbytes = _workspace_for(p.device, rows, cols)
+    def _muon_batch(self, items, rows, cols):
+        """One kernel-4 step over matrices of one shape (optimizer.py:52-61 per matrix)."""
+        dev = items[0][0].device
+        batch = len(items)
+        nbytes = _lib.lib().mb_muon_batch_workspace_bytes(batch, rows, cols)
+        ws = _WS.get(dev, nbytes)
         f = lambda x: float(np.float32(x))  # noqa: E731
         args = _lib.MuonArgs(f(.05), f(.95), f(NS_COEFFS[0]), f(NS_COEFFS[1]), f(NS_COEFFS[2]), 5,
-                             f(max(1, p.shape[0] / p.shape[1]) ** .5), f(1 - self.lr * self.weight_decay),
+                             f(max(1, rows / cols) ** .5), f(1 - self.lr * self.weight_decay),
                              f(-self.lr), ns_operand_dtype(rows, cols, self.ns_dtype))
-        out, odt = None, _lib.MB_NONE
+        odt = _lib.MB_NONE
+        outs = None
         if self.low_precision is not None:
-            out = self.low_precision_copies.get(p)
-            if out is None:
-                out = torch.empty_like(p, dtype=self.low_precision)
-                self.low_precision_copies[p] = out
             odt = _lib.dtype_code(self.low_precision)
-        err = torch.zeros(1, dtype=torch.int32, device=p.device)
-        with torch.cuda.device(p.device):
-            _lib.check(_lib.lib().mb_muon_step(
-                _lib.ptr(p), _lib.ptr(momentum), _lib.ptr(g), _lib.dtype_code(g.dtype),
-                None if out is None else _lib.ptr(out), odt, rows, cols, ctypes.byref(args), _lib.ptr(ws), nbytes,
-                _lib.ptr(err), _lib.stream_handle()), "muon_step")
+            outs = []
+            for p, _, _ in items:
+                out = self.low_precision_copies.get(p)
+                if out is None:
+                    out = self.low_precision_copies[p] = torch.empty_like(p, dtype=self.low_precision)
+                outs.append(_lib.ptr(out))
+        table = ctypes.c_void_p * batch
+        err = self._err.get(dev)
+        if err is None:
+            err = self._err[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(_lib.lib().mb_muon_step_batched(
+                table(*[_lib.ptr(p) for p, _, _ in items]), table(*[_lib.ptr(m) for _, m, _ in items]),
+                table(*[_lib.ptr(g) for _, _, g in items]), _lib.dtype_code(items[0][2].dtype),
+                None if outs is None else table(*outs), odt, batch, rows, cols, ctypes.byref(args), _lib.ptr(ws),
+                nbytes, _lib.ptr(err), _lib.stream_handle()), "muon_step")
 
     def state_dict(self):
         return dict(momentum=self.momentum, adam=self.adam.state_dict(), lr=self.lr, weight_decay=self.weight_decay)

@@ -140,3 +140,115 @@ def test_orthogonalize_full_size_bf16_vs_torch_fp32(cuda, shape):
         torch.backends.cuda.matmul.allow_tf32 = prev
     err = float((out - x).norm() / x.norm())
     assert err < 1e-2, err
+
+
+def _muon_args(rows, cols, ns_dtype, lr=.02, wd=.01):
+    from morph_b200 import _lib
+    from morph_b200.muon import NS_COEFFS
+    f = lambda x: float(np.float32(x))  # noqa: E731
+    return _lib.MuonArgs(f(.05), f(.95), f(NS_COEFFS[0]), f(NS_COEFFS[1]), f(NS_COEFFS[2]), 5,
+                         f(max(1, rows / cols) ** .5), f(1 - lr * wd), f(-lr), ns_dtype)
+
+
+@pytest.mark.parametrize("shape", [(300, 520), (520, 300), (256, 1024), (40, 72)])
+@pytest.mark.parametrize("gdt", [torch.float32, torch.bfloat16])
+def test_batched_step_bit_identical_to_one_matrix_calls(cuda, shape, gdt):
+    """mb_muon_step_batched gives each matrix exactly mb_muon_step's result."""
+    import ctypes
+    from morph_b200 import _lib
+    rows, cols = shape
+    batch = 5
+    gen = torch.Generator(device=cuda).manual_seed(rows + cols)
+    w0 = [torch.randn(shape, device=cuda, generator=gen) for _ in range(batch)]
+    m0 = [torch.randn(shape, device=cuda, generator=gen) * .1 for _ in range(batch)]
+    gs = [(torch.randn(shape, device=cuda, generator=gen) * 1e-3).to(gdt) for _ in range(batch)]
+    ns = _lib.MB_F16 if min(shape) < 256 else _lib.MB_BF16
+    args = _muon_args(rows, cols, ns)
+    lib = _lib.lib()
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    # one call per matrix
+    w1, m1 = [w.clone() for w in w0], [m.clone() for m in m0]
+    o1 = [torch.empty(shape, dtype=torch.bfloat16, device=cuda) for _ in range(batch)]
+    n1 = lib.mb_muon_workspace_bytes(rows, cols)
+    ws1 = torch.empty(n1, dtype=torch.uint8, device=cuda)
+    for b in range(batch):
+        _lib.check(lib.mb_muon_step(_lib.ptr(w1[b]), _lib.ptr(m1[b]), _lib.ptr(gs[b]), _lib.dtype_code(gdt),
+                                    _lib.ptr(o1[b]), _lib.MB_BF16, rows, cols, ctypes.byref(args), _lib.ptr(ws1), n1,
+                                    _lib.ptr(err), _lib.stream_handle()))
+    # one batched call
+    w2, m2 = [w.clone() for w in w0], [m.clone() for m in m0]
+    o2 = [torch.empty(shape, dtype=torch.bfloat16, device=cuda) for _ in range(batch)]
+    n2 = lib.mb_muon_batch_workspace_bytes(batch, rows, cols)
+    ws2 = torch.empty(n2, dtype=torch.uint8, device=cuda)
+    table = ctypes.c_void_p * batch
+    _lib.check(lib.mb_muon_step_batched(table(*map(_lib.ptr, w2)), table(*map(_lib.ptr, m2)),
+                                        table(*map(_lib.ptr, gs)), _lib.dtype_code(gdt), table(*map(_lib.ptr, o2)),
+                                        _lib.MB_BF16, batch, rows, cols, ctypes.byref(args), _lib.ptr(ws2), n2,
+                                        _lib.ptr(err), _lib.stream_handle()))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for b in range(batch):
+        assert torch.equal(w1[b], w2[b]) and torch.equal(m1[b], m2[b]) and torch.equal(o1[b], o2[b]), b
+        assert torch.equal(o2[b], w2[b].bfloat16())
+    # and each matrix against the FP32 oracle
+    for b in (0, batch - 1):
+        g = gs[b].float().cpu().numpy()
+        mom = m0[b].cpu().numpy().copy()
+        u = orc.muon_momentum_(mom, g)
+        np.testing.assert_array_equal(m2[b].cpu().numpy(), mom)
+        w_ref = w0[b].cpu().numpy().copy()
+        orc.muon_apply_(w_ref, orc.orthogonalize(u), .02, .01)
+        decay = w0[b].cpu().numpy() * np.float32(1 - .02 * .01)
+        assert _rel(w2[b].cpu().numpy() - decay, w_ref - decay) < 1e-2
+
+
+def test_batched_step_rejects_bad_arguments(cuda):
+    import ctypes
+    from morph_b200 import _lib
+    lib = _lib.lib()
+    assert lib.mb_muon_batch_workspace_bytes(0, 64, 64) == 0
+    assert lib.mb_muon_batch_workspace_bytes(_lib.MB_MUON_MAX_BATCH + 1, 64, 64) == 0
+    assert lib.mb_muon_batch_workspace_bytes(_lib.MB_MUON_MAX_BATCH, 64, 64) > 0
+    w = torch.zeros(64, 64, device=cuda)
+    args = _muon_args(64, 64, _lib.MB_F16)
+    n = lib.mb_muon_batch_workspace_bytes(2, 64, 64)
+    ws = torch.empty(n, dtype=torch.uint8, device=cuda)
+    table = ctypes.c_void_p * 2
+    good = table(_lib.ptr(w), _lib.ptr(w))
+    bad = table(_lib.ptr(w), None)
+    rc = lib.mb_muon_step_batched(good, bad, good, _lib.MB_F32, None, _lib.MB_NONE, 2, 64, 64, ctypes.byref(args),
+                                  _lib.ptr(ws), n, None, _lib.stream_handle())
+    assert rc == _lib.MB_ERR_ARG
+    rc = lib.mb_muon_step_batched(good, good, good, _lib.MB_F32, None, _lib.MB_NONE, 2, 64, 64, ctypes.byref(args),
+                                  _lib.ptr(ws), n - 1, None, _lib.stream_handle())
+    assert rc == _lib.MB_ERR_ARG
+
+
+def test_hybrid_batches_by_shape_match_one_matrix_batches(cuda):
+    """HybridMuonAdamW groups same-shape matrices into batched launches; a
+    workspace limit of one byte forces one matrix per launch: same bits."""
+    from morph_b200 import HybridMuonAdamW
+
+    def build():
+        torch.manual_seed(3)
+        return torch.nn.Sequential(*[torch.nn.Linear(96, 64, bias=False) for _ in range(5)],
+                                   torch.nn.Linear(64, 160, bias=False), torch.nn.Linear(160, 64, bias=False),
+                                   torch.nn.LayerNorm(64)).to(cuda)
+
+    models = [build(), build()]
+    opts = [HybridMuonAdamW(models[0], lr=.02, low_precision=torch.bfloat16),
+            HybridMuonAdamW(models[1], lr=.02, low_precision=torch.bfloat16, workspace_limit=1)]
+    gen = torch.Generator(device=cuda).manual_seed(0)
+    for _ in range(3):
+        grads = [torch.randn(p.shape, device=cuda, generator=gen) * 1e-2 for p in models[0].parameters()]
+        for model, opt in zip(models, opts):
+            for p, g in zip(model.parameters(), grads):
+                p.grad = g.clone()
+            opt.step()
+    for p, q in zip(models[0].parameters(), models[1].parameters()):
+        assert torch.equal(p, q)
+    for i in opts[0].momentum:
+        assert torch.equal(opts[0].momentum[i], opts[1].momentum[i])
+    for p, q in zip(opts[0].muon, opts[1].muon):
+        assert torch.equal(opts[0].low_precision_copies[p], opts[1].low_precision_copies[q])
+        assert torch.equal(opts[0].low_precision_copies[p], p.detach().bfloat16())
