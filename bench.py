@@ -385,17 +385,10 @@ def run_ns_only(args):
                       "tflops_executed": ns_flops_executed(rows, cols) / (ms / 1e3) / 1e12}), flush=True)
 
 
-def run_config4(args):
-    """Config 4: hybrid Muon + AdamW at the 7B shape, one GPU. Muon: 32 layers x
-    {3 x [4096, 11008], 4 x [4096, 4096]} FP32 masters and momentum, BF16 grads
-    N(0, 1e-4), Newton-Schulz 5 iterations on BF16 tcgen05 GEMMs. AdamW: a
-    [65536, 4096] embedding and 64 vectors [4096]. Prints one JSON line with the
-    step time and the Newton-Schulz tensor throughput per matrix shape."""
-    import ctypes
-    from morph_b200 import HybridMuonAdamW, _lib
-    from morph_b200.muon import NS_COEFFS
-    device = torch.device("cuda", 0)
-    torch.cuda.set_device(device)
+def config4_model(device):
+    """Config 4's parameters (random init) with seeded BF16 gradients N(0, 1e-4):
+    32 layers x {3 x [4096, 11008], 4 x [4096, 4096]} Linear weights, a
+    [65536, 4096] embedding and 64 vectors [4096]. Every rank builds the same."""
 
     class Model(torch.nn.Module):
         def __init__(self):
@@ -415,6 +408,75 @@ def run_config4(args):
     for p in model.parameters():
         p.grad_dtype = None
         p.grad = (torch.randn(p.shape, device=device, generator=gen) * 1e-4).to(torch.bfloat16)
+    return model
+
+
+CONFIG4_WORKLOAD = ("config4: Muon 32 x {3 x [4096,11008], 4 x [4096,4096]} + AdamW [65536,4096] + 64 x [4096]")
+
+
+def run_config4_zero(args, rank, world, local_rank):
+    """Config 4 on N GPUs: ZeroHybridMuonAdamW (whole Muon matrices dealt over
+    the ranks, AdamW group flat-sharded, BF16 weights all-gathered per round).
+    Time per step = max over ranks of the device-timed step."""
+    import torch.distributed as dist
+    from morph_b200.zero import ZeroHybridMuonAdamW
+    device = torch.device("cuda", local_rank)
+    model = config4_model(device)
+    opt = ZeroHybridMuonAdamW(model, lr=3e-4, weight_decay=.1, ns_dtype="bf16", device=device)
+    grads = [p.grad for p in model.parameters()]
+    for _ in range(args.warmup):
+        opt.step(grads)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        start.record()
+        for _ in range(args.steps):
+            opt.step(grads)
+        stop.record()
+        torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([start.elapsed_time(stop) / args.steps], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms = float(t.item())
+    total_flop = sum(ns_flops(*q.shape) for q in opt.muon)
+    peaks = {}
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    if rank == 0:
+        achieved = total_flop / (step_ms / 1e3) / 1e12
+        line = {"metric": "Hybrid Muon+AdamW step (config 4, 7B shape)", "value": step_ms / 1e3, "unit": "s/step",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+                "higher_is_better": False, "scaling": "strong", "dtype": "bf16 NS operands, f32 state",
+                "data": "synthetic",
+                "config": {"workload": CONFIG4_WORKLOAD, "parallelism": f"muon-matrix-shard + zero1-dp{world}",
+                           "muon_matrices_per_rank": len(opt.owned), "rounds": len(opt.rounds)},
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak * world,
+                             "peak_kind": "measured sustained x n_gpus" if peaks else "fallback x n_gpus",
+                             "unit": "TFLOP/s", "frac": achieved / (peak * world),
+                             "basis": "whole step time, algorithmic NS FLOPs"},
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+
+
+def run_config4(args):
+    """Config 4: hybrid Muon + AdamW at the 7B shape, one GPU. Muon: 32 layers x
+    {3 x [4096, 11008], 4 x [4096, 4096]} FP32 masters and momentum, BF16 grads
+    N(0, 1e-4), Newton-Schulz 5 iterations on BF16 tcgen05 GEMMs. AdamW: a
+    [65536, 4096] embedding and 64 vectors [4096]. Prints one JSON line with the
+    step time and the Newton-Schulz tensor throughput per matrix shape."""
+    import ctypes
+    from morph_b200 import HybridMuonAdamW, _lib
+    from morph_b200.muon import NS_COEFFS
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+
+    model = config4_model(device)
     opt = HybridMuonAdamW(model, lr=3e-4, weight_decay=.1, ns_dtype="bf16")
     muon_params = sum(p.numel() for p in opt.muon)
     adam_params = sum(p.numel() for g in opt.adam.param_groups for p in g["params"])
@@ -480,8 +542,7 @@ def run_config4(args):
     line = {"metric": "Hybrid Muon+AdamW step (config 4, 7B shape)", "value": step_ms / 1e3, "unit": "s/step",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
             "higher_is_better": False, "dtype": "bf16 NS operands, f32 state", "data": "synthetic",
-            "config": {"workload": "config4: Muon 32 x {3 x [4096,11008], 4 x [4096,4096]} + AdamW "
-                                   "[65536,4096] + 64 x [4096]", "muon_params": muon_params,
+            "config": {"workload": CONFIG4_WORKLOAD, "muon_params": muon_params,
                        "adam_params": adam_params, "ns_flop_per_step": total_flop},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "peak_kind": "measured sustained" if peaks else "fallback", "unit": "TFLOP/s",
@@ -543,19 +604,27 @@ def reference_rows_cpu_time(rows_k, cols, steps=2):
     return times, threads
 
 
-def run_config5(args):
+def run_config5(args, rank=0, world=1, local_rank=0):
     """Config 5: lazy row-sparse AdamW with the [262144, 3072] table's w, m, v in
     pinned host memory, 10% of rows (sorted unique int64) touched per step with
     FP16 grads N(0, 1e-3), DiskState.update hyperparameters (lr 1e-4, clip 1.0),
-    256 MiB ping-pong windows. Metric: touched params/s; roofline: host link."""
-    from morph_b200.offload import OffloadedRowTable
-    device = torch.device("cuda", 0)
+    256 MiB ping-pong windows. Metric: touched params/s; roofline: host link.
+    N > 1: the rows are sharded in contiguous blocks (ShardedRowTable), each GPU
+    streams its block over its own host link; time = max over ranks."""
+    from morph_b200.offload import OffloadedRowTable, ShardedRowTable
+    device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     rows, cols, k = 262144, 3072, 26214
     gen = torch.Generator().manual_seed(1234)
     init = torch.empty(rows, cols)
     init.normal_(0.0, 0.02, generator=gen)
-    table = OffloadedRowTable(rows, cols, init=init, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        table = ShardedRowTable(rows, cols, init=init, device=device)
+        window_rows = table.local.window_rows
+    else:
+        table = OffloadedRowTable(rows, cols, init=init, device=device)
+        window_rows = table.window_rows
     del init
     steps = args.warmup + args.steps
     idxs, grads = [], []
@@ -567,30 +636,47 @@ def run_config5(args):
     for step in range(args.warmup):
         table.step(idxs[step], grads[step], step + 1, 1e-4, 1.0)
     table.synchronize()
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(0) as clk:
+    with ClockSampler(local_rank) as clk:
         start.record()
         for step in range(args.warmup, steps):
             table.step(idxs[step], grads[step], step + 1, 1e-4, 1.0)
         stop.record()
         table.synchronize()
     ms = start.elapsed_time(stop) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
     link_bytes = 24 * k * cols
-    link = host_link_gbs(device)
+    link = host_link_gbs(device)  # every rank at once: the links' aggregate
+    if world > 1:
+        agg = torch.tensor([link["h2d"], link["d2h"], link["both"]], device=device, dtype=torch.float64)
+        dist.all_reduce(agg)
+        link = {"h2d": float(agg[0]), "d2h": float(agg[1]), "both": float(agg[2]), "ranks_concurrent": world}
     achieved = link_bytes / (ms / 1e3) / 1e9
-    ref_times, threads = reference_rows_cpu_time(k, cols)
+    if rank != 0:
+        return
     line = {"metric": "lazy row-sparse AdamW on pinned-host state (config 5)", "value": k * cols / (ms / 1e3),
-            "unit": "touched params/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms, "higher_is_better": True, "dtype": "f32 state, f16 grads", "data": "synthetic",
+            "unit": "touched params/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "dtype": "f32 state, f16 grads",
+            "data": "synthetic",
             "config": {"workload": "config5: [262144,3072] table, 26214 rows/step, 256 MiB windows",
-                       "window_rows": table.window_rows, "touched_params": k * cols},
+                       "window_rows": window_rows, "touched_params": k * cols,
+                       "parallelism": "single GPU" if world == 1 else f"row-block shard over {world} GPUs"},
             "roofline": {"bound": "host link", "achieved": achieved, "peak": link["both"],
                          "unit": "GB/s", "frac": achieved / link["both"],
                          "algorithmic_link_bytes_per_step": link_bytes, "link_measured": link},
-            "cpu_baseline": {"value": k * cols / (sum(ref_times) / len(ref_times)), "unit": "touched params/s",
-                             "cores": threads, "kind": "reference",
-                             "sample": "disk.py:210-215 arithmetic on the gathered [26214, 3072] rows in RAM"},
             "clocks": clk.summary()}
+    if world == 1:
+        ref_times, threads = reference_rows_cpu_time(k, cols)
+        line["cpu_baseline"] = {"value": k * cols / (sum(ref_times) / len(ref_times)), "unit": "touched params/s",
+                                "cores": threads, "kind": "reference",
+                                "sample": "disk.py:210-215 arithmetic on the gathered [26214, 3072] rows in RAM"}
     print(json.dumps(line), flush=True)
 
 
@@ -787,10 +873,10 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
-    if args.config == 4:
+    if args.config == 4 and (args.ns_shape or world == 1):
         run_ns_only(args) if args.ns_shape else run_config4(args)
         return
-    if args.config == 5:
+    if args.config == 5 and world == 1:
         run_config5(args)
         return
     if world > 1:
@@ -800,7 +886,11 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if world > 1:
+        if world > 1 and args.config == 4:
+            run_config4_zero(args, rank, world, local_rank)
+        elif world > 1 and args.config == 5:
+            run_config5(args, rank, world, local_rank)
+        elif world > 1:
             run_morph_zero(args, rank, world, local_rank)
         else:
             run_morph(args, rank, world, local_rank)

@@ -120,6 +120,64 @@ def orthogonalize(gradient: torch.Tensor, steps: int = 5, ns_dtype="auto") -> to
     return out
 
 
+def batch_plan(count, rows, cols, workspace_limit):
+    """Sizes of the batches that step ``count`` [rows, cols] matrices: as few
+    launches as the workspace limit and MB_MUON_MAX_BATCH allow, evenly filled."""
+    if count <= 0:
+        return []
+    per = _lib.lib().mb_muon_batch_workspace_bytes(1, rows, cols)
+    if per == 0:
+        raise ValueError(f"unsupported matrix shape {(rows, cols)}")
+    cap = max(1, min(_lib.MB_MUON_MAX_BATCH, int(workspace_limit) // per))
+    n = -(-count // cap)
+    size = -(-count // n)
+    return [min(size, count - b) for b in range(0, count, size)]
+
+
+def muon_step_batched(params, moms, grads, outs, lr, weight_decay, ns_dtype="auto", err=None):
+    """optimizer.py:52-61 for each of ``params`` (same-shape contiguous FP32 CUDA
+    matrices on one device) in one kernel-4 call: momentum (FP32, in place),
+    Nesterov blend, Newton-Schulz, shape scale, decoupled weight decay; ``outs``
+    (optional, one 16-bit tensor each) receive the updated weights. ``err``
+    (int32 device flag) is raised when a bounded wait expires."""
+    batch = len(params)
+    if batch == 0:
+        return
+    rows, cols = params[0].shape
+    dev = params[0].device
+    gdt = grads[0].dtype
+    for p, m, g in zip(params, moms, grads):
+        if (p.dim() != 2 or not p.is_cuda or p.dtype != torch.float32 or not p.is_contiguous()
+                or tuple(p.shape) != (rows, cols) or p.device != dev):
+            raise ValueError("Muon parameters must be contiguous same-shape 2-D float32 CUDA tensors")
+        if m.shape != p.shape or m.dtype != torch.float32 or not m.is_contiguous():
+            raise ValueError("momentum must match its parameter")
+        if g.shape != p.shape or g.dtype != gdt or not g.is_contiguous():
+            raise ValueError("gradients must be contiguous, of the parameter's shape and one dtype")
+    if outs is not None:
+        for o in outs:
+            if (o.shape != (rows, cols) or not o.is_contiguous() or o.dtype != outs[0].dtype
+                    or o.dtype not in (torch.bfloat16, torch.float16)):
+                raise ValueError("copies must be contiguous BF16 or FP16 tensors of the parameters' shape")
+    nbytes = _lib.lib().mb_muon_batch_workspace_bytes(batch, rows, cols)
+    if nbytes == 0:
+        raise ValueError(f"unsupported batch {batch} of {(rows, cols)}")
+    ws = _WS.get(dev, nbytes)
+    f = lambda x: float(np.float32(x))  # noqa: E731
+    args = _lib.MuonArgs(f(.05), f(.95), f(NS_COEFFS[0]), f(NS_COEFFS[1]), f(NS_COEFFS[2]), 5,
+                         f(max(1, rows / cols) ** .5), f(1 - lr * weight_decay), f(-lr),
+                         ns_operand_dtype(rows, cols, ns_dtype))
+    odt = _lib.MB_NONE if outs is None else _lib.dtype_code(outs[0].dtype)
+    table = ctypes.c_void_p * batch
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().mb_muon_step_batched(
+            table(*[_lib.ptr(p) for p in params]), table(*[_lib.ptr(m) for m in moms]),
+            table(*[_lib.ptr(g) for g in grads]), _lib.dtype_code(gdt),
+            None if outs is None else table(*[_lib.ptr(o) for o in outs]), odt, batch, rows, cols,
+            ctypes.byref(args), _lib.ptr(ws), nbytes, None if err is None else _lib.ptr(err),
+            _lib.stream_handle()), "muon_step")
+
+
 def partition(model):
     """streamtrain/optimizer.py:25-31: weights of nn.Linear modules not named
     'lm_head' go to Muon, every other parameter to AdamW."""
@@ -207,46 +265,28 @@ class HybridMuonAdamW:
             g = p.grad.contiguous()
             groups.setdefault((p.device, tuple(p.shape), g.dtype), []).append((p, self.momentum[i], g))
         for (dev, (rows, cols), _), items in groups.items():
-            per = _lib.lib().mb_muon_batch_workspace_bytes(1, rows, cols)
-            if per == 0:
-                raise ValueError(f"unsupported matrix shape {(rows, cols)}")
-            cap = max(1, min(_lib.MB_MUON_MAX_BATCH, self.workspace_limit // per))
-            n_batches = -(-len(items) // cap)
-            size = -(-len(items) // n_batches)
-            for b in range(0, len(items), size):
+            b = 0
+            for size in batch_plan(len(items), rows, cols, self.workspace_limit):
                 self._muon_batch(items[b:b + size], rows, cols)
+                b += size
         self.adam.step()
 
     def _muon_batch(self, items, rows, cols):
         """One kernel-4 step over matrices of one shape (optimizer.py:52-61 per matrix)."""
         dev = items[0][0].device
-        batch = len(items)
-        nbytes = _lib.lib().mb_muon_batch_workspace_bytes(batch, rows, cols)
-        ws = _WS.get(dev, nbytes)
-        f = lambda x: float(np.float32(x))  # noqa: E731
-        args = _lib.MuonArgs(f(.05), f(.95), f(NS_COEFFS[0]), f(NS_COEFFS[1]), f(NS_COEFFS[2]), 5,
-                             f(max(1, rows / cols) ** .5), f(1 - self.lr * self.weight_decay),
-                             f(-self.lr), ns_operand_dtype(rows, cols, self.ns_dtype))
-        odt = _lib.MB_NONE
         outs = None
         if self.low_precision is not None:
-            odt = _lib.dtype_code(self.low_precision)
             outs = []
             for p, _, _ in items:
                 out = self.low_precision_copies.get(p)
                 if out is None:
                     out = self.low_precision_copies[p] = torch.empty_like(p, dtype=self.low_precision)
-                outs.append(_lib.ptr(out))
-        table = ctypes.c_void_p * batch
+                outs.append(out)
         err = self._err.get(dev)
         if err is None:
             err = self._err[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
-        with torch.cuda.device(dev):
-            _lib.check(_lib.lib().mb_muon_step_batched(
-                table(*[_lib.ptr(p) for p, _, _ in items]), table(*[_lib.ptr(m) for _, m, _ in items]),
-                table(*[_lib.ptr(g) for _, _, g in items]), _lib.dtype_code(items[0][2].dtype),
-                None if outs is None else table(*outs), odt, batch, rows, cols, ctypes.byref(args), _lib.ptr(ws),
-                nbytes, _lib.ptr(err), _lib.stream_handle()), "muon_step")
+        muon_step_batched([p for p, _, _ in items], [m for _, m, _ in items], [g for _, _, g in items], outs,
+                          self.lr, self.weight_decay, self.ns_dtype, err)
 
     def state_dict(self):
         return dict(momentum=self.momentum, adam=self.adam.state_dict(), lr=self.lr, weight_decay=self.weight_decay)

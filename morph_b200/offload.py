@@ -63,3 +63,44 @@ class OffloadedRowTable:
         if int(self._err.item()):
             self._err.zero_()
             raise IndexError("row index out of range")
+
+
+class ShardedRowTable:
+    """An offloaded row table sharded by contiguous row blocks over the ranks of
+    a process group, one GPU (and its own host link) per rank.
+
+    Rank r owns rows [rows*r/N, rows*(r+1)/N) in its own ``OffloadedRowTable``.
+    ``step`` takes the full sorted index list and gradient rows (as every rank
+    holds them after the gradient reduction) and updates the contiguous slice of
+    the list that falls in this rank's block; the arithmetic per row is exactly
+    the unsharded table's, and no collective is needed."""
+
+    def __init__(self, rows: int, cols: int, init=None, device="cuda", window_bytes: int = 256 << 20,
+                 process_group=None, table_factory=None):
+        import torch.distributed as dist
+        self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
+        self.rows, self.cols = int(rows), int(cols)
+        self.lo = self.rows * self.rank // self.world
+        self.hi = self.rows * (self.rank + 1) // self.world
+        block = None if init is None else torch.as_tensor(init).reshape(self.rows, self.cols)[self.lo:self.hi]
+        make = table_factory or (lambda r, c, i: OffloadedRowTable(r, c, init=i, device=device,
+                                                                  window_bytes=window_bytes))
+        self.local = make(self.hi - self.lo, self.cols, block)
+
+    def local_slice(self, index: torch.Tensor):
+        """(a, b): the positions of this rank's rows in the sorted index list."""
+        bounds = torch.tensor([self.lo, self.hi], dtype=index.dtype, device=index.device)
+        a, b = torch.searchsorted(index, bounds).tolist()
+        return a, b
+
+    def step(self, index: torch.Tensor, grads: torch.Tensor, step: int, lr: float, clip: float = 1.0,
+             loss_scale: float = 1.0) -> int:
+        """Update this rank's rows of ``index``; returns how many rows that was."""
+        a, b = self.local_slice(index)
+        if b > a:
+            self.local.step(index[a:b] - self.lo, grads[a:b], step, lr, clip, loss_scale)
+        return b - a
+
+    def synchronize(self) -> None:
+        self.local.synchronize()

@@ -252,3 +252,217 @@ class ZeroAdamW:
         return dict(rank=self.rank, world=self.world, rounds=self.rounds, chunk=self.cs, chunks=self.chunks,
                     master=self.master.cpu(), exp_avg=self.exp_avg.cpu(), exp_avg_sq=self.exp_avg_sq.cpu(),
                     lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.weight_decay)
+
+
+# ----------------------------------------------------- Hybrid Muon + AdamW ----
+
+def deal_matrices(shapes, world, rank_batches):
+    """Whole-matrix sharding of the Muon group.
+
+    shapes: the Muon matrices' shapes in order. Matrices of one shape are dealt
+    round-robin over the ranks (one shape = one Newton-Schulz cost, so every rank
+    gets the same FLOPs up to one matrix per shape). ``rank_batches(count, rows,
+    cols)`` gives the batch sizes one rank uses for ``count`` matrices of a shape.
+    Returns the rounds: a list of {rank: [matrix index, ...]}; in every round each
+    rank steps one batch of one shape, so the rounds line up across ranks."""
+    groups = {}
+    for i, s in enumerate(shapes):
+        groups.setdefault(tuple(s), []).append(i)
+    rounds = []
+    for shape, idx in groups.items():
+        per_rank = [idx[r::world] for r in range(world)]
+        sizes = rank_batches(len(per_rank[0]), *shape)  # rank 0 holds the most
+        b = 0
+        for size in sizes:
+            rounds.append({r: per_rank[r][b:b + size] for r in range(world)})
+            b += size
+    return rounds
+
+
+class CudaHybridBackend:
+    """Kernel calls of one sharded Hybrid step on the rank's GPU (C-ABI library)."""
+
+    def __init__(self, device, ns_dtype="auto"):
+        self.device = torch.device(device)
+        self.engine = StepEngine(self.device)
+        self.ns_dtype = ns_dtype
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._keys = {}
+
+    def gate_record(self, grads) -> torch.Tensor:
+        """Kernel 2 over ``grads``: the {sumsq, nonfinite} record (2 x FP64 on the device)."""
+        rec = self.engine.state_buf[:16].view(torch.float64)
+        if not grads:
+            rec.zero_()
+            return rec
+        gdt = grads[0].dtype
+        flat = [g.reshape(-1) for g in grads]
+        keys = self._keys.get(len(flat))  # clock slots are unused by the statistics; reuse them
+        if keys is None:
+            keys = self._keys[len(flat)] = [object() for _ in flat]
+            for k in keys:
+                self.engine.slot(k, 0)
+        entries = [(g, g, g, g, None, 0) for g in flat]
+        plan = self.engine.prepare(entries, [(0.0, .9, .9, 1e-8, 0.0, "torch")], _lib.dtype_code(gdt), _lib.MB_NONE,
+                                   keys=keys)
+        with torch.cuda.device(self.device):
+            _lib.check(self.engine.lib.mb_grad_stats(ctypes.byref(plan), None, _lib.stream_handle()), "mb_grad_stats")
+        return rec
+
+    def muon_batch(self, params, moms, grads, outs, lr, weight_decay):
+        from .muon import muon_step_batched
+        muon_step_batched(params, moms, grads, outs, lr, weight_decay, self.ns_dtype, self.err)
+
+    def check_errors(self):
+        if int(self.err.item()):
+            self.err.zero_()
+            raise RuntimeError("muon step: a bounded wait expired on the device")
+
+
+class ZeroHybridMuonAdamW:
+    """HybridMuonAdamW (streamtrain/optimizer.py:34-70) sharded over the GPUs of
+    one node, one process per GPU.
+
+    The Muon matrices are sharded whole (Newton-Schulz needs the full matrix):
+    ``deal_matrices`` gives each rank the same number of matrices of each shape.
+    Rank r keeps the FP32 masters and momentum of its matrices; the AdamW group
+    (embedding, norms, biases) is a ``ZeroAdamW`` over the flat space. Every rank
+    holds the full low-precision weights (``weights``, one tensor per parameter
+    in ``params`` order). One step:
+
+      1. kernel 2 (finiteness) over this rank's Muon gradients and its AdamW
+         chunks; all_reduce of the 16-byte record; every rank raises
+         FloatingPointError, changing nothing, if any gradient is not finite
+         (optimizer.py:50-51);
+      2. per round: this rank's batch of one shape through kernel 4, writing the
+         BF16 copies into place, then all_gather_into_tensor of the round's
+         block (in place, on NCCL's stream) while the next round computes;
+      3. the AdamW group's ZeRO-1 step (kernels 2 + 1, its own all-gathers).
+
+    ``params`` are the model's parameters; ``muon`` selects the Muon ones
+    (default: ``partition(model)`` when ``model`` is given)."""
+
+    def __init__(self, model=None, lr=1e-3, muon_lr=None, weight_decay=.01, *, params=None, muon=None,
+                 low_precision=torch.bfloat16, process_group=None, device=None, backend=None, adam_backend=None,
+                 ns_dtype="auto", workspace_limit=4 << 30, adam_rounds=4):
+        from .muon import batch_plan, partition
+        if model is not None:
+            muon_list, adam_list = partition(model)
+            params = list(model.parameters())
+        else:
+            params = list(params)
+            ids = {id(p) for p in (muon or [])}
+            muon_list = [p for p in params if id(p) in ids]
+            adam_list = [p for p in params if id(p) not in ids]
+        if not params:
+            raise ValueError("ZeroHybridMuonAdamW needs parameters")
+        self.group = process_group
+        self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
+        self.device = torch.device(device) if device is not None else params[0].device
+        self.lr = lr if muon_lr is None else muon_lr
+        self.weight_decay = weight_decay
+        self.low_precision = low_precision
+        self.params = params
+        self.muon = muon_list
+        self.adam_params = adam_list
+        for p in self.muon:
+            if p.dim() != 2:
+                raise ValueError("Muon parameters must be 2-D")
+        self.backend = backend if backend is not None else CudaHybridBackend(self.device, ns_dtype)
+        if backend is None:
+            plan = lambda n, r, c: batch_plan(n, r, c, workspace_limit)  # noqa: E731
+        else:
+            plan = getattr(backend, "batch_plan", lambda n, r, c: [n] if n else [])
+        self.rounds = deal_matrices([tuple(p.shape) for p in self.muon], self.world, plan)
+        # flat low-precision buffer of the Muon group: per round, one equal block per rank
+        self.layout = {}  # muon index -> (round, offset in the flat buffer)
+        self.round_blocks = []  # (offset, block elements per rank)
+        off = 0
+        for k, rd in enumerate(self.rounds):
+            per = max(sum(self.muon[i].numel() for i in rd[r]) for r in range(self.world))
+            per = -(-per // ALIGN) * ALIGN
+            for r in range(self.world):
+                o = off + r * per
+                for i in rd[r]:
+                    self.layout[i] = (k, o)
+                    o += self.muon[i].numel()
+            self.round_blocks.append((off, per))
+            off += per * self.world
+        self.flat_muon = torch.zeros(max(off, 1), dtype=low_precision, device=self.device)
+        self.muon_weights = [self.flat_muon[o:o + p.numel()].view(p.shape)
+                             for p, (_, o) in ((self.muon[i], self.layout[i]) for i in range(len(self.muon)))]
+        self.owned = [i for rd in self.rounds for i in rd[self.rank]]
+        self.master = {i: self.muon[i].detach().to(self.device, torch.float32).clone() for i in self.owned}
+        self.momentum = {}
+        for i in range(len(self.muon)):  # every rank starts from the full weights
+            self.muon_weights[i].copy_(self.muon[i].detach().to(self.device))
+        self.adam = ZeroAdamW(adam_list, lr=lr, betas=(.9, .95), eps=1e-8, weight_decay=weight_decay,
+                              low_precision=low_precision, process_group=process_group, device=self.device,
+                              backend=adam_backend, rounds=adam_rounds) if adam_list else None
+        index = {id(p): i for i, p in enumerate(self.muon)}
+        aindex = {id(p): i for i, p in enumerate(adam_list)}
+        self.weights = [self.muon_weights[index[id(p)]] if id(p) in index else self.adam.weights[aindex[id(p)]]
+                        for p in params]
+
+    def _gather(self, k):
+        off, per = self.round_blocks[k]
+        block = self.flat_muon[off:off + per * self.world]
+        own = block[self.rank * per:(self.rank + 1) * per]
+        return dist.all_gather_into_tensor(block, own, group=self.group, async_op=True)
+
+    @torch.no_grad()
+    def step(self, grads=None) -> None:
+        """One step. ``grads``: the full, already reduced gradients in ``params``
+        order (default: each parameter's ``.grad``); Muon gradients of one shape
+        share a dtype."""
+        grads = [p.grad for p in self.params] if grads is None else list(grads)
+        if len(grads) != len(self.params):
+            raise ValueError("one gradient per parameter expected")
+        gmap = {id(p): g for p, g in zip(self.params, grads)}
+        muon_grads = [gmap[id(p)] for p in self.muon]
+        adam_grads = [gmap[id(p)] for p in self.adam_params]
+        if any(g is None for g in muon_grads + adam_grads):
+            raise ValueError("every parameter needs a gradient")
+        muon_grads = [g.to(self.device).contiguous() for g in muon_grads]
+        # 1. finiteness over this rank's share, one decision on every rank
+        own_grads = [muon_grads[i] for i in self.owned]
+        if self.adam is not None:
+            for i, t_off, _, n, _ in self.adam.pieces:
+                own_grads.append(adam_grads[i].reshape(-1)[t_off:t_off + n])
+        by_dtype = {}
+        for g in own_grads:
+            by_dtype.setdefault(g.dtype, []).append(g)
+        rec = torch.zeros(2, dtype=torch.float64, device=self.device)
+        for gs in by_dtype.values():
+            rec += self.backend.gate_record(gs)
+        if self.world > 1:
+            dist.all_reduce(rec, group=self.group)
+        if float(rec[1].item()) != 0.0:
+            raise FloatingPointError('nonfinite gradient; optimizer not updated')
+        self.backend.check_errors()
+        # 2. Muon rounds, each all-gathered while the next computes
+        works = []
+        for k, rd in enumerate(self.rounds):
+            mine = rd[self.rank]
+            if mine:
+                for i in mine:
+                    if i not in self.momentum:
+                        self.momentum[i] = torch.zeros_like(self.master[i])
+                self.backend.muon_batch([self.master[i] for i in mine], [self.momentum[i] for i in mine],
+                                        [muon_grads[i] for i in mine], [self.muon_weights[i] for i in mine],
+                                        self.lr, self.weight_decay)
+            if self.world > 1:
+                works.append(self._gather(k))
+        # 3. the AdamW group
+        if self.adam is not None:
+            self.adam.step(adam_grads)
+        for w in works:
+            w.wait()
+
+    def state_dict(self) -> dict:
+        """This rank's share: Muon masters and momentum by Muon index, the AdamW shard."""
+        return dict(rank=self.rank, world=self.world, lr=self.lr, weight_decay=self.weight_decay,
+                    master={i: t.cpu() for i, t in self.master.items()},
+                    momentum={i: t.cpu() for i, t in self.momentum.items()},
+                    adam=self.adam.state_dict() if self.adam is not None else None)

@@ -43,3 +43,62 @@ def test_offloaded_rows_out_of_range_reported(cuda):
     with pytest.raises(IndexError):
         table.synchronize()
     assert table.w[3].abs().sum() > 0 or table.m[3].abs().sum() > 0
+
+
+def _sharded_worker(rank, world, port, q):
+    import datetime
+    import os
+    import torch.distributed as dist
+    from morph_b200.offload import ShardedRowTable
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        dev = torch.device("cuda", rank)
+        rows, cols = 500, 96
+        w0 = orc.rng(5).standard_normal((rows, cols), dtype=np.float32) * np.float32(.02)
+        t = ShardedRowTable(rows, cols, init=w0, device=dev, window_bytes=9 * 3 * cols * 4)
+        r = orc.rng(6)
+        for step in (1, 2):
+            idx = np.sort(r.choice(rows, 60, replace=False)).astype(np.int64)
+            g = torch.from_numpy(r.standard_normal((60, cols), dtype=np.float32) * np.float32(1e-3)).half()
+            t.step(torch.from_numpy(idx).to(dev), g.to(dev), step, 1e-4, clip=.5)
+        t.synchronize()
+        q.put((rank, (t.lo, t.hi, t.local.w.numpy().copy(), t.local.m.numpy().copy())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_sharded_two_gpus_equal_oracle(cuda):
+    """Two GPUs, each with its own pinned block of rows: every row bit-exact with
+    the oracle's unsharded update."""
+    import socket
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_sharded_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    rows, cols = 500, 96
+    w = orc.rng(5).standard_normal((rows, cols), dtype=np.float32) * np.float32(.02)
+    m, v = np.zeros_like(w), np.zeros_like(w)
+    r = orc.rng(6)
+    for step in (1, 2):
+        idx = np.sort(r.choice(rows, 60, replace=False)).astype(np.int64)
+        g = torch.from_numpy(r.standard_normal((60, cols), dtype=np.float32) * np.float32(1e-3)).half()
+        orc.sparse_rows_(w, m, v, idx, orc.grad_prepare(g.float().numpy(), coef=.5), orc.disk_scalars(1e-4, step))
+    for rank in (0, 1):
+        lo, hi, wl, ml = res[rank]
+        np.testing.assert_array_equal(wl, w[lo:hi])
+        np.testing.assert_array_equal(ml, m[lo:hi])
+    assert res[0][1] == res[1][0] and res[1][1] == rows
