@@ -23,6 +23,11 @@
  *   mb_sparse_rows_update
  *       the conditional AdamW of streamtrain/sparse_disk.py:122-138 applied to the
  *       touched rows of one table (DiskState.update on the gathered rows).
+ *   mb_grad_accumulate
+ *       the microbatch accumulation g.float() / loss_scale into the FP32 gradient
+ *       window of streamtrain/sparse_disk.py:82-110, with the norm statistics.
+ *   mb_export_f16
+ *       the FP16 export cast and range check of streamtrain/export.py:30-35.
  *   mb_cast_f32
  *       the FP32 -> BF16/FP16 compute copy (streamtrain/disk.py:320-326,351) and the
  *       FP16 export with its range check (streamtrain/export.py:32-34).
@@ -309,6 +314,27 @@ MB_API int mb_fp8_pack(const float* src, int64_t n, uint8_t* codes, float* scale
  * out_dtype (MB_F32, MB_F16 or MB_BF16). */
 MB_API int mb_fp8_unpack(const uint8_t* codes, const float* scales, int64_t n, void* out, int32_t out_dtype,
                          mb_stream_t stream);
+
+/* Microbatch gradient accumulation (streamtrain/sparse_disk.py:82-110):
+ * acc = acc + f32(g) / loss_scale over n elements (first != 0: acc = 0 +
+ * f32(g) / loss_scale, i.e. the window's zero_() fused in), IEEE division.
+ * With record != NULL (device, 2 doubles) the call also adds
+ * {sum of acc^2 in FP64, 1 if any acc value is nonfinite} of the updated acc
+ * to record (the norm pass of sparse_disk.py:119-120 / disk.py:466-468), in a
+ * fixed reduction order; workspace (device, mb_accumulate_workspace_bytes(),
+ * zeroed once before first use) is then required. Calls that share a
+ * workspace must be ordered on one stream. */
+MB_API size_t mb_accumulate_workspace_bytes(void);
+MB_API int mb_grad_accumulate(float* acc, const void* g, int32_t grad_dtype, int64_t n, float loss_scale,
+                              int32_t first, double* record, void* workspace, mb_stream_t stream);
+
+/* FP16 export of n FP32 values (streamtrain/export.py:30-35): dst (device
+ * memory, or pinned host memory written through its device mapping) receives
+ * the values rounded to nearest even; *first_bad (device memory, set by the
+ * caller to UINT64_MAX beforehand) is lowered to the index of the first value
+ * that is nonfinite or has |x| > 65504. Elements before that index are always
+ * written. */
+MB_API int mb_export_f16(const float* src, int64_t n, void* dst, uint64_t* first_bad, mb_stream_t stream);
 
 /* FP32 -> F16/BF16 cast (round to nearest even). With check != 0 (F16 only)
  * a nonfinite value or |x| > 65504 sets *err_flag to 1 (export.py:33). */

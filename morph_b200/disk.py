@@ -138,3 +138,54 @@ def cast_f32(src: torch.Tensor, dtype: torch.dtype, export_check: bool = False) 
     if export_check and int(err.item()):
         raise ValueError('weights cannot be represented by finite FP16')
     return dst
+
+
+class _AccWorkspace:
+    """Per-device scratch of mb_grad_accumulate's statistics (zeroed once)."""
+
+    def __init__(self):
+        self.buf = {}
+
+    def get(self, device):
+        t = self.buf.get(device)
+        if t is None:
+            t = self.buf[device] = torch.zeros(_lib.lib().mb_accumulate_workspace_bytes(), dtype=torch.uint8,
+                                               device=device)
+        return t
+
+
+_ACC_WS = _AccWorkspace()
+
+
+def norm_record(device) -> torch.Tensor:
+    """A zeroed device record {sum of squares, nonfinite} (2 x FP64) for accumulate_."""
+    return torch.zeros(2, dtype=torch.float64, device=device)
+
+
+def accumulate_(acc: torch.Tensor, gradient: torch.Tensor, loss_scale: float = 1.0, *, first: bool = False,
+                record: torch.Tensor = None) -> torch.Tensor:
+    """acc.add_(gradient.float() / loss_scale) on the device, the microbatch
+    accumulation of streamtrain/sparse_disk.py:82-110 (``first=True`` is the
+    window's zero_() followed by the first add). With ``record`` (from
+    ``norm_record``) the same pass adds the updated acc's FP64 sum of squares and
+    a nonfinite flag to it, the statistics of the norm pass
+    (sparse_disk.py:119-120). Calls on one device must share one stream."""
+    if not acc.is_cuda or acc.dtype != torch.float32 or not acc.is_contiguous():
+        raise ValueError("acc must be a contiguous float32 CUDA tensor")
+    if gradient.shape != acc.shape or gradient.device != acc.device or not gradient.is_contiguous():
+        raise ValueError("gradient must be contiguous, on acc's device and of acc's shape")
+    if record is not None and (record.dtype != torch.float64 or record.numel() != 2 or record.device != acc.device):
+        raise ValueError("record must be a 2-element float64 tensor on acc's device")
+    with torch.cuda.device(acc.device):
+        _lib.check(_lib.lib().mb_grad_accumulate(
+            _lib.ptr(acc), _lib.ptr(gradient), _lib.dtype_code(gradient.dtype), acc.numel(), float(loss_scale),
+            int(bool(first)), None if record is None else _lib.ptr(record),
+            _lib.ptr(_ACC_WS.get(acc.device)) if record is not None else None, _lib.stream_handle()),
+            "grad_accumulate")
+    return acc
+
+
+def record_norm(record: torch.Tensor) -> float:
+    """sqrt of the accumulated sum of squares (inf/nan when a value was nonfinite)."""
+    s, bad = record.tolist()
+    return float("nan") if bad else math.sqrt(s)

@@ -211,6 +211,28 @@ def export_f16(x: np.ndarray) -> np.ndarray:
     return out
 
 
+def export_f16_chunks(x: np.ndarray, chunk_elements=1048576):
+    """export.py:30-35 for one tensor: (bytes the reference writes, whether it
+    raised). Chunks are checked in order; the first bad chunk raises after the
+    chunks before it were written."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    out = []
+    for start in range(0, x.size, chunk_elements):
+        value = x[start:start + chunk_elements]
+        if not np.isfinite(value).all() or np.abs(value).max(initial=0) > 65504:
+            return b"".join(out), True
+        out.append(value.astype('<f2').tobytes())
+    return b"".join(out), False
+
+
+def grad_accumulate_(acc: np.ndarray, g32: np.ndarray, loss_scale=1.0, first=False) -> None:
+    """sparse_disk.py:82-110: the window is zeroed, then each microbatch adds
+    g.float() / loss_scale (float32 division and addition)."""
+    if first:
+        acc[...] = np.float32(0)
+    acc += np.asarray(g32, np.float32) / np.float32(loss_scale)
+
+
 def sparse_rows_(w, m, v, idx, grads32, scalars: Scalars):
     """DiskState.update applied to the gathered rows ``idx`` of [rows, cols] planes."""
     rows, cols = w.shape

@@ -217,3 +217,31 @@ def test_oracle_fp8_matches_reference(golden):
     x = golden["fp8_in"]
     back = orc.unpack_fp8(codes, scales, "float32")
     assert np.linalg.norm(back - x) / np.linalg.norm(x) < .04  # tests/test_fp16.py:16-19
+
+
+@pytest.mark.parametrize("scale", [1.0, 1024.0, 3.7])
+def test_oracle_accumulate_matches_reference_torch_ops(scale):
+    """sparse_disk.py:82-110 run literally with torch on the CPU: zero_() the
+    window, then destination.add_(g.detach().float() / loss_scale) per microbatch."""
+    r = orc.rng(17)
+    grads = [torch.from_numpy(r.standard_normal(5003).astype(np.float32) * 30).half() for _ in range(4)]
+    grads[1][7] = -0.0
+    dest = torch.empty(5003).fill_(123.0)
+    dest.zero_()
+    for g in grads:
+        dest.add_(g.detach().float() / scale)
+    acc = np.full(5003, 123.0, np.float32)
+    for k, g in enumerate(grads):
+        orc.grad_accumulate_(acc, g.float().numpy(), scale, first=k == 0)
+    np.testing.assert_array_equal(acc.view(np.uint32), dest.numpy().view(np.uint32))
+
+
+def test_oracle_export_chunks_follow_the_reference_order():
+    x = orc.rng(18).standard_normal(10_007).astype(np.float32)
+    data, raised = orc.export_f16_chunks(x, 1000)
+    assert not raised and data == x.astype('<f2').tobytes()
+    x[5500] = 70000.0
+    data, raised = orc.export_f16_chunks(x, 1000)
+    assert raised and data == x[:5000].astype('<f2').tobytes()
+    x[0] = np.nan
+    assert orc.export_f16_chunks(x, 1000) == (b"", True)
