@@ -28,12 +28,36 @@ from __future__ import annotations
 
 import ctypes
 import os
+from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 import torch
 
 from . import _lib
 from .disk import disk_host_scalars
+
+
+_POOL = None
+
+
+def _pool():
+    """Host copy threads (numpy releases the GIL while copying)."""
+    global _POOL
+    if _POOL is None:
+        _POOL = ThreadPoolExecutor(max_workers=max(1, min(8, os.cpu_count() or 1)))
+    return _POOL
+
+
+def _parallel_copy(dst: np.ndarray, src: np.ndarray, pieces: int = 8) -> None:
+    """dst[...] = src for (3, n) arrays, split by columns over the host threads."""
+    n = dst.shape[1]
+    step = max(1, -(-n // pieces))
+    if n <= step or n < (1 << 16):
+        np.copyto(dst, src)
+        return
+    futures = [_pool().submit(np.copyto, dst[:, a:a + step], src[:, a:a + step]) for a in range(0, n, step)]
+    for f in futures:
+        f.result()
 
 
 class GpuDiskUpdater:
@@ -95,7 +119,7 @@ class GpuDiskUpdater:
             n = min(W, size - lo)
             host = self.host[b][:3 * n].view(3, n)
             dev = self.dev[b][:3 * n].view(3, n)
-            np.copyto(host.numpy(), mapped[:, lo:lo + n])  # buffer b was written back already
+            _parallel_copy(host.numpy(), mapped[:, lo:lo + n])  # buffer b was written back already
             with torch.cuda.stream(self.h2d):
                 if j >= 2:
                     self.h2d.wait_event(self.done[b])  # device window b's copy-back is complete
@@ -126,7 +150,7 @@ class GpuDiskUpdater:
             host = self.host[b][:3 * n].view(3, n).numpy()
             for c0 in range(0, n, chunk_elements):  # the reference's write and fault granularity
                 c1 = min(c0 + chunk_elements, n)
-                mapped[:, lo + c0:lo + c1] = host[:, c0:c1]
+                _parallel_copy(mapped[:, lo + c0:lo + c1], host[:, c0:c1])
                 self._fault('partial_state_write')
 
         stage(0)
