@@ -109,7 +109,7 @@ typedef struct mb_step_state {
   double norm;            /* sqrt(sumsq) of the last finalized step             */
   float clip_coef;        /* multiplier applied to unscaled gradients           */
   int32_t skip;           /* 1 if the last finalized step skips its update      */
-  int32_t status;         /* MB_OK, MB_ERR_OVERFLOW_MIN_SCALE or MB_ERR_NONFINITE*/
+  int32_t status;         /* MB_OK, MB_ERR_OVERFLOW_MIN_SCALE, MB_ERR_NONFINITE or MB_ERR_TIMEOUT */
   int32_t steps_applied;  /* updates applied so far                             */
   int32_t steps_skipped;  /* updates skipped so far                             */
   int32_t reserved[3];

@@ -16,10 +16,13 @@
 // (16-bit) run. The grid is persistent (CTAs resident on all SMs) and strides
 // over tiles.
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <utility>
 
+#include "mb_async.cuh"
 #include "mb_common.cuh"
 
 // Compile-time tuning knob: minimum resident CTAs per SM requested from ptxas
@@ -122,8 +125,8 @@ __device__ __forceinline__ bool seg_vec_ok(const mb_segment& seg, int gdt, int o
 // before any arithmetic or store (112 B in flight per thread for BF16 grads).
 template <int GDT, int ODT>
 __device__ __forceinline__ void apply_tile(const mb_segment& seg, int64_t tile_in_seg, bool vec,
-                                           const StepScalars& s, const GradPrep& prep) {
-  const int64_t e0 = tile_in_seg * kTile + threadIdx.x * kQuad;
+                                           const StepScalars& s, const GradPrep& prep, int tid) {
+  const int64_t e0 = tile_in_seg * kTile + tid * kQuad;
   const int64_t e1 = e0 + kHalf;
   if (vec && e1 + kQuad <= seg.numel) {
     float g0[4], g1[4];
@@ -180,8 +183,186 @@ __global__ void __launch_bounds__(kThreads, MB_APPLY_MIN_BLOCKS) k_adamw_apply(A
       s = group_scalars(a.groups[seg.group], a.seg_scal[si]);
       vec = seg_vec_ok(seg, GDT, ODT);
     }
-    apply_tile<GDT, ODT>(seg, tile - seg.tile_begin, vec, s, prep);
+    apply_tile<GDT, ODT>(seg, tile - seg.tile_begin, vec, s, prep, threadIdx.x);
   }
+}
+
+// Kernel 1, bulk-staged form (plan mode). One persistent CTA per SM: warp 0's
+// lane 0 streams each tile's w, m, v and gradient into a ring of shared-memory
+// stages with cp.async.bulk (completion counted in mbarrier transaction
+// bytes); eight consumer warps read a stage into registers, release it, run
+// the same element arithmetic and store w, m, v (and the low-precision copy)
+// straight to global memory. The ring keeps up to kBulkStages tiles of reads in
+// flight per SM independent of the consumers' registers. Tiles whose segment
+// is not 16-byte aligned, or whose partial length is not a multiple of 8, take
+// the direct-load path inside the consumers (the producer only signals them).
+// Every wait is bounded; on expiry the CTA stops and records MB_ERR_TIMEOUT in
+// the step state.
+#ifndef MB_BULK_STAGES
+#define MB_BULK_STAGES 3
+#endif
+#ifndef MB_BULK_WARPS
+#define MB_BULK_WARPS 4
+#endif
+#ifndef MB_BULK_CTAS
+#define MB_BULK_CTAS 2
+#endif
+constexpr int kBulkStages = MB_BULK_STAGES;        // ring depth (tiles)
+constexpr int kBulkConsumerWarps = MB_BULK_WARPS;  // consumers; each thread takes kBulkQuads quads of a tile
+constexpr int kBulkCtasPerSm = MB_BULK_CTAS;
+constexpr int kBulkThreads = 32 * (kBulkConsumerWarps + 1);
+constexpr int kBulkQuads = kTile / (kQuad * 32 * kBulkConsumerWarps);
+static_assert(kBulkQuads * kQuad * 32 * kBulkConsumerWarps == kTile, "consumers must tile a tile exactly");
+
+template <int GDT>
+__host__ __device__ constexpr int bulk_stage_bytes() {
+  return kTile * (12 + (GDT == MB_F32 ? 4 : 2));
+}
+template <int GDT>
+__host__ __device__ constexpr int bulk_smem_bytes() {
+  return kBulkStages * bulk_stage_bytes<GDT>() + 2 * kBulkStages * 8 + 16;
+}
+
+// Segment cursor of a CTA role: tiles only grow, so the segment advances; the
+// next segment's first tile is cached, so most tiles touch no table entry.
+struct SegCursor {
+  int cur = -1;
+  int64_t next_begin = -1;  // first tile of segment cur + 1 (INT64_MAX past the last)
+  __device__ __forceinline__ bool advance(const ApplyArgs& a, int64_t tile) {
+    if (cur >= 0 && tile < next_begin) return false;
+    int si = cur < 0 ? find_segment(a.segs, a.n_segs, tile) : cur;
+    while (si + 1 < a.n_segs && __ldg(&a.segs[si + 1].tile_begin) <= tile) ++si;
+    next_begin = si + 1 < a.n_segs ? __ldg(&a.segs[si + 1].tile_begin) : INT64_MAX;
+    const bool changed = si != cur;
+    cur = si;
+    return changed;
+  }
+};
+
+__device__ __forceinline__ bool bulk_ok(const mb_segment& seg, int gdt, int odt, int64_t n) {
+  return seg_vec_ok(seg, gdt, odt) && aligned(seg.g, 16) && (n == kTile || n % 8 == 0);
+}
+
+template <int GDT, int ODT>
+__global__ void __launch_bounds__(kBulkThreads, kBulkCtasPerSm) k_adamw_apply_bulk(ApplyArgs a) {
+  constexpr int GB = GDT == MB_F32 ? 4 : 2;
+  constexpr int STAGE = bulk_stage_bytes<GDT>();
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBulkStages * STAGE);
+  uint64_t* empty = full + kBulkStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kBulkStages);
+  mb_step_state* st = const_cast<mb_step_state*>(a.state);  // the plan's device record
+  if (st->skip) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kBulkStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kBulkConsumerWarps);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) {
+      SegCursor sc_;
+      mb_segment seg;
+      int k = 0;
+      int last_bulk[kBulkStages];  // per stage, the tile count k of its last bulk fill (-1: none)
+#pragma unroll
+      for (int i = 0; i < kBulkStages; ++i) last_bulk[i] = -1;
+      for (int64_t tile = a.tile_lo + blockIdx.x; tile < a.n_tiles; tile += gridDim.x, ++k) {
+        if (sc_.advance(a, tile)) seg = a.segs[sc_.cur];
+        const int s = k % kBulkStages;
+        if (!mbar_wait(&empty[s], ((k / kBulkStages) & 1) ^ 1, abort_flag)) break;
+        const int64_t t = tile - seg.tile_begin;
+        const int64_t e = t * kTile;
+        const int64_t rest = seg.numel - e;
+        const int n = (int)(rest < kTile ? rest : kTile);
+        if (bulk_ok(seg, GDT, ODT, n)) {
+          uint8_t* base = smem + s * STAGE;
+          mbar_expect_tx(&full[s], (uint32_t)n * (12 + GB));
+          bulk_load(base, seg.w + e, n * 4, &full[s]);
+          bulk_load(base + kTile * 4, seg.m + e, n * 4, &full[s]);
+          bulk_load(base + kTile * 8, seg.v + e, n * 4, &full[s]);
+          bulk_load(base + kTile * 12, static_cast<const uint8_t*>(seg.g) + e * GB, n * GB, &full[s]);
+          last_bulk[s] = k;
+        } else {
+          mbar_arrive(&full[s]);
+        }
+      }
+      if (*abort_flag) {
+        // give the copies still in flight (bounded) time to land before the CTA's shared memory goes away
+#pragma unroll
+        for (int i = 0; i < kBulkStages; ++i) {
+          if (last_bulk[i] < 0) continue;
+          const uint32_t parity = (last_bulk[i] / kBulkStages) & 1;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&full[i], parity) && globaltimer() - t0 < kWaitLimitNs) {
+          }
+        }
+      }
+    }
+  } else {
+    const int ct = threadIdx.x - 32;
+    GradPrep prep = make_prep(__double2float_rn(st->step_scale), st->clip_coef);
+    SegCursor sc_;
+    mb_segment seg;
+    StepScalars sc;
+    int k = 0;
+    for (int64_t tile = a.tile_lo + blockIdx.x; tile < a.n_tiles; tile += gridDim.x, ++k) {
+      if (sc_.advance(a, tile)) {
+        seg = a.segs[sc_.cur];
+        sc = group_scalars(a.groups[seg.group], a.seg_scal[sc_.cur]);
+      }
+      const int s = k % kBulkStages;
+      if (!mbar_wait(&full[s], (k / kBulkStages) & 1, abort_flag)) break;
+      const int64_t t = tile - seg.tile_begin;
+      const int64_t e = t * kTile;
+      const int64_t rest = seg.numel - e;
+      const int n = (int)(rest < kTile ? rest : kTile);
+      if (!bulk_ok(seg, GDT, ODT, n)) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        // the direct path covers a tile with 256 threads x 2 quads
+        for (int part = ct; part < kThreads; part += 32 * kBulkConsumerWarps)
+          apply_tile<GDT, ODT>(seg, t, seg_vec_ok(seg, GDT, ODT), sc, prep, part);
+        continue;
+      }
+      const uint8_t* base = smem + s * STAGE;
+      float4 w4[kBulkQuads], m4[kBulkQuads], v4[kBulkQuads];
+      float g4[kBulkQuads][4];
+      bool in[kBulkQuads];
+#pragma unroll
+      for (int q = 0; q < kBulkQuads; ++q) {
+        const int qe = (q * 32 * kBulkConsumerWarps + ct) * kQuad;  // element offset in the tile
+        in[q] = qe < n;  // n % 8 == 0 or a full tile: a quad is all in or all out
+        if (in[q]) {
+          w4[q] = *reinterpret_cast<const float4*>(base + qe * 4);
+          m4[q] = *reinterpret_cast<const float4*>(base + kTile * 4 + qe * 4);
+          v4[q] = *reinterpret_cast<const float4*>(base + kTile * 8 + qe * 4);
+          load4_any<GDT>(base + kTile * 12, qe, g4[q]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+      for (int q = 0; q < kBulkQuads; ++q) {
+        if (!in[q]) continue;
+        const int64_t ge = e + (q * 32 * kBulkConsumerWarps + ct) * kQuad;
+        float ww[4] = {w4[q].x, w4[q].y, w4[q].z, w4[q].w}, mm[4] = {m4[q].x, m4[q].y, m4[q].z, m4[q].w};
+        float vv[4] = {v4[q].x, v4[q].y, v4[q].z, v4[q].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) adam_elem(ww[j], mm[j], vv[j], prep(g4[q][j]), sc);
+        st4f(seg.w + ge, make_float4(ww[0], ww[1], ww[2], ww[3]));
+        st4f(seg.m + ge, make_float4(mm[0], mm[1], mm[2], mm[3]));
+        st4f(seg.v + ge, make_float4(vv[0], vv[1], vv[2], vv[3]));
+        if constexpr (ODT != MB_NONE) store4<ODT>(seg.out, ge, ww);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(&st->status, MB_ERR_TIMEOUT);
 }
 
 // Kernel 1 (single tensor, host scalars): DiskState.update on device memory.
@@ -194,7 +375,8 @@ __global__ void __launch_bounds__(kThreads) k_adamw_update(mb_segment seg, int64
   s.cwd = hs.cwd; s.b2 = hs.beta2; s.omb2 = hs.omb2; s.eps = hs.eps; s.nss = hs.nss; s.bc2s = hs.bc2s;
   GradPrep prep = make_prep(hs.scale, hs.coef);
   bool vec = seg_vec_ok(seg, GDT, ODT);
-  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) apply_tile<GDT, ODT>(seg, tile, vec, s, prep);
+  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x)
+    apply_tile<GDT, ODT>(seg, tile, vec, s, prep, threadIdx.x);
 }
 
 // ------------------------------------------------------------- kernel 2 --
@@ -459,6 +641,66 @@ ApplyFn pick_apply(int gdt, int odt) {
     default: return nullptr;
   }
 }
+struct BulkFn {
+  ApplyFn fn;
+  int smem;
+};
+template <int GDT>
+BulkFn pick_apply_bulk(int odt) {
+  switch (odt) {
+    case MB_NONE: return {&k_adamw_apply_bulk<GDT, MB_NONE>, bulk_smem_bytes<GDT>()};
+    case MB_F16: return {&k_adamw_apply_bulk<GDT, MB_F16>, bulk_smem_bytes<GDT>()};
+    case MB_BF16: return {&k_adamw_apply_bulk<GDT, MB_BF16>, bulk_smem_bytes<GDT>()};
+    default: return {nullptr, 0};
+  }
+}
+BulkFn pick_apply_bulk(int gdt, int odt) {
+  switch (gdt) {
+    case MB_F32: return pick_apply_bulk<MB_F32>(odt);
+    case MB_F16: return pick_apply_bulk<MB_F16>(odt);
+    case MB_BF16: return pick_apply_bulk<MB_BF16>(odt);
+    default: return {nullptr, 0};
+  }
+}
+
+// Kernel 1's form: the bulk-staged kernel unless MB_APPLY_KERNEL=direct
+// selects the register-staged one (read once).
+bool use_bulk_apply() {
+  static const bool bulk = [] {
+    const char* e = getenv("MB_APPLY_KERNEL");
+    return !(e && strcmp(e, "direct") == 0);
+  }();
+  return bulk;
+}
+
+// Opt a bulk kernel into its dynamic shared memory (once per kernel and device).
+bool bulk_ready(ApplyFn fn, int smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, bool> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(reinterpret_cast<const void*>(fn), dev);
+  auto it = done.find(key);
+  if (it != done.end()) return it->second;
+  bool ok = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess;
+  done[key] = ok;
+  return ok;
+}
+
+int sm_count() {
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (sms[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev] = n > 0 ? n : 148;
+  }
+  return sms[dev];
+}
+
 template <int GDT>
 UpdateFn pick_update(int odt) {
   switch (odt) {
@@ -592,6 +834,7 @@ MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* p, int64_t tile_lo, int64_t
   if (tile_lo == tile_hi) return MB_OK;
   ApplyFn fn = pick_apply(p->grad_dtype, p->out_dtype);
   if (!fn) return MB_ERR_ARG;
+  BulkFn bulk = pick_apply_bulk(p->grad_dtype, p->out_dtype);
   ApplyArgs a;
   a.segs = p->segs;
   a.groups = p->groups;
@@ -600,6 +843,14 @@ MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* p, int64_t tile_lo, int64_t
   a.tile_lo = tile_lo;
   a.n_tiles = tile_hi;
   a.n_segs = p->n_segs;
+  if (use_bulk_apply() && bulk.fn && bulk_ready(bulk.fn, bulk.smem)) {
+    // kBulkCtasPerSm CTAs per SM; max_ctas counts register-staged CTAs (3 per SM)
+    int64_t grid = (int64_t)sm_count() * kBulkCtasPerSm;
+    if (max_ctas > 0) grid = max_ctas * kBulkCtasPerSm / 3 > 0 ? max_ctas * kBulkCtasPerSm / 3 : 1;
+    if (grid > tile_hi - tile_lo) grid = tile_hi - tile_lo;
+    bulk.fn<<<(int)grid, kBulkThreads, bulk.smem, (cudaStream_t)stream>>>(a);
+    return launch_status();
+  }
   int grid = grid_for(reinterpret_cast<const void*>(fn), tile_hi - tile_lo);
   if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
   fn<<<grid, kThreads, 0, (cudaStream_t)stream>>>(a);

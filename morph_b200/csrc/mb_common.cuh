@@ -67,6 +67,25 @@ template <> __device__ __forceinline__ void load4<MB_BF16>(const void* p, int64_
   x[2] = __uint_as_float(q.y << 16); x[3] = __uint_as_float(q.y & 0xffff0000u);
 }
 
+// The same 4 elements from any address space (plain loads; for shared memory,
+// which the global-only streaming loads above cannot address).
+template <int DT> __device__ __forceinline__ void load4_any(const void* p, int64_t e, float (&x)[4]);
+template <> __device__ __forceinline__ void load4_any<MB_F32>(const void* p, int64_t e, float (&x)[4]) {
+  float4 q = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + e);
+  x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
+}
+template <> __device__ __forceinline__ void load4_any<MB_F16>(const void* p, int64_t e, float (&x)[4]) {
+  uint2 q = *reinterpret_cast<const uint2*>(static_cast<const __half*>(p) + e);
+  __half2 a = *reinterpret_cast<__half2*>(&q.x), b = *reinterpret_cast<__half2*>(&q.y);
+  float2 fa = __half22float2(a), fb = __half22float2(b);
+  x[0] = fa.x; x[1] = fa.y; x[2] = fb.x; x[3] = fb.y;
+}
+template <> __device__ __forceinline__ void load4_any<MB_BF16>(const void* p, int64_t e, float (&x)[4]) {
+  uint2 q = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p) + e);
+  x[0] = __uint_as_float(q.x << 16); x[1] = __uint_as_float(q.x & 0xffff0000u);
+  x[2] = __uint_as_float(q.y << 16); x[3] = __uint_as_float(q.y & 0xffff0000u);
+}
+
 template <int DT> __device__ __forceinline__ float load1(const void* p, int64_t e) {
   return to_f32(static_cast<const typename Elem<DT>::T*>(p)[e]);
 }

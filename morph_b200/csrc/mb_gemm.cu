@@ -38,6 +38,7 @@
 
 #include <mutex>
 
+#include "mb_async.cuh"
 #include "mb_common.cuh"
 
 namespace mb {
@@ -51,7 +52,6 @@ constexpr int B_STAGE = BN * BK * 2;   // 32 KiB
 constexpr int kBarrierBytes = 256;  // full/empty rings, 2 x acc full/empty, TMEM slot, abort flag
 constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + 1024 + kBarrierBytes;
 constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 // Instruction descriptor, kind::f16: D FP32 (bits 4-5 = 1), A and B of one
 // 16-bit type (bits 7-9 and 10-12: 1 = BF16, 0 = FP16), both K-major (bits 15,
@@ -88,51 +88,6 @@ struct Args {
   void* upd_out[kMaxBatch];
   int32_t* err;
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Wait for the phase of `parity` to complete; false on abort or time-out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
-      *abort_flag = 1;
-      return false;
-    }
-  }
-}
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
   asm volatile(
