@@ -43,7 +43,7 @@ STATS_BYTES = 2    # kernel 2: g 2 R
 # Kernel 1's DRAM traffic per parameter, dram__bytes_read.sum + dram__bytes_write.sum
 # from one ncu capture of a one-layer launch (1.321411 GB + 1.263679 GB over
 # 94,384,128 params); traffic grows in proportion to the parameters processed.
-APPLY_TRAFFIC_PER_PARAM = (1.321411e9 + 1.263679e9) / 94384128
+APPLY_TRAFFIC_PER_PARAM = (1.321469e9 + 1.264979e9) / 94384128  # ncu, k_adamw_apply_bulk, one layer
 FALLBACK_HBM_GBS = 6650.0
 
 
