@@ -22,6 +22,7 @@ a per-parameter compute copy written by the same kernel).
 """
 from __future__ import annotations
 
+import collections
 import ctypes
 import math
 
@@ -102,6 +103,8 @@ class StepEngine:
     tables, the kernel workspace and the step-state record (its own, or the
     one of an attached DynamicLossScale)."""
 
+    SEG_CACHE = 4  # distinct segment tables kept on the device
+
     def __init__(self, device, loss_scale: DynamicLossScale | None = None):
         self.device = torch.device(device)
         self.lib = _lib.lib()
@@ -120,9 +123,9 @@ class StepEngine:
             _lib.check(self.lib.mb_step_state_init(ctypes.byref(st), 1.0, 1 << 62))
             self.state_buf = torch.frombuffer(bytearray(bytes(st)), dtype=torch.uint8).to(self.device)
         self.workspace = None
-        self._seg_key = None
-        self._segs_dev = None
-        self._n_tiles = 0
+        # device segment tables of the last few distinct layouts (a caller that
+        # alternates gradient buffers alternates between two of them)
+        self._seg_cache = collections.OrderedDict()
         self._group_bytes = None
         self._groups_dev = None
 
@@ -136,7 +139,7 @@ class StepEngine:
             grown[: self.clocks.numel()] = self.clocks
             self.clocks = grown
             self.generation += 1
-            self._seg_key = None
+            self.invalidate_segments()
 
     def slot(self, p: torch.Tensor, initial_clock: int = 0) -> int:
         key = id(p)
@@ -175,19 +178,24 @@ class StepEngine:
         key = tuple((p.data_ptr(), m.data_ptr(), v.data_ptr(), g.data_ptr(),
                      0 if o is None else o.data_ptr(), g.numel(), sl, gi)
                     for (p, m, v, g, o, gi), sl in zip(entries, slots))
-        if key != self._seg_key:
+        hit = self._seg_cache.get(key)
+        if hit is None:
             segs = np.zeros(n, _SEG_DTYPE)
             tiles = 0
             for i, ((p, m, v, g, o, gi), sl) in enumerate(zip(entries, slots)):
                 segs[i] = (p.data_ptr(), m.data_ptr(), v.data_ptr(), g.data_ptr(),
                            0 if o is None else o.data_ptr(), g.numel(), tiles, sl, gi)
                 tiles += (g.numel() + TILE - 1) // TILE
-            self._segs_dev = _to_device_bytes(segs, self.device)
-            self._n_tiles = tiles
-            self._seg_key = key
+            hit = (_to_device_bytes(segs, self.device), tiles)
+            self._seg_cache[key] = hit
+            while len(self._seg_cache) > self.SEG_CACHE:
+                self._seg_cache.popitem(last=False)
             need = self.lib.mb_workspace_bytes(n)
             if self.workspace is None or self.workspace.numel() < need:
                 self.workspace = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        else:
+            self._seg_cache.move_to_end(key)
+        segs_dev, n_tiles = hit
         garr = np.zeros(len(groups), _GROUP_DTYPE)
         for i, (lr, b1, b2, eps, wd, kind) in enumerate(groups):
             garr[i] = (lr, np.float32(1 - lr * wd), np.float32(1 - b1), np.float32(b2), np.float32(1 - b2),
@@ -197,9 +205,13 @@ class StepEngine:
             self._groups_dev = _to_device_bytes(garr, self.device)
             self._group_bytes = gbytes
         bc, bc_len = self.tables.ensure(self.max_clock + 1)
-        return _lib.Plan(self._segs_dev.data_ptr(), self._groups_dev.data_ptr(), bc.data_ptr(),
+        return _lib.Plan(segs_dev.data_ptr(), self._groups_dev.data_ptr(), bc.data_ptr(),
                          self.clocks.data_ptr(), self.workspace.data_ptr(), self.state_buf.data_ptr(),
-                         self._n_tiles, bc_len, n, len(groups), grad_dtype, out_dtype)
+                         n_tiles, bc_len, n, len(groups), grad_dtype, out_dtype)
+
+    def invalidate_segments(self) -> None:
+        """Forget the cached segment tables (clock slots or layouts changed)."""
+        self._seg_cache.clear()
 
     @staticmethod
     def finalize_opts(fin_flags, max_norm) -> _lib.FinalizeOpts:
@@ -389,4 +401,4 @@ class AdamW(torch.optim.Optimizer):
                         eng.set_clock(p, int(float(st["step"])))
                         st["step"] = eng.clock_view(p)
         if self._engine is not None:
-            self._engine._seg_key = None
+            self._engine.invalidate_segments()
