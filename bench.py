@@ -43,6 +43,7 @@ STATS_BYTES = 2    # kernel 2: g 2 R
 # Kernel 1's DRAM traffic per parameter, dram__bytes_read.sum + dram__bytes_write.sum
 # from one ncu capture of a one-layer launch (1.321411 GB + 1.263679 GB over
 # 94,384,128 params); traffic grows in proportion to the parameters processed.
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (B200, NVLink 5)
 APPLY_TRAFFIC_PER_PARAM = (1.321469e9 + 1.264979e9) / 94384128  # ncu, k_adamw_apply_bulk, one layer
 FALLBACK_HBM_GBS = 6650.0
 
@@ -848,7 +849,7 @@ def run_morph_zero(args, rank, world, local_rank):
         params.append(full[off:off + n].view(shape))
         off += n
     opt = ZeroAdamW(params, LR, BETAS, EPS, WD, max_norm=MAX_NORM, gate=True, device=device, rounds=args.rounds,
-                    reserve_sms=args.reserve_sms)
+                    reserve_sms=args.reserve_sms, peer_writes=False if args.no_peer_writes else "auto")
     del params, full
     torch.cuda.empty_cache()
     gflat = torch.empty(total, dtype=torch.bfloat16, device=device)
@@ -921,6 +922,30 @@ def run_morph_zero(args, rank, world, local_rank):
 
     hbm, peak_kind = measured_peaks()
     achieved = APPLY_BYTES * owned / (apply_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "mb_adamw_apply_tiles", "achieved": achieved, "peak": hbm,
+                "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
+                "algorithmic_bytes_per_launch": APPLY_BYTES * owned,
+                "traffic": APPLY_TRAFFIC_PER_PARAM * owned,
+                "traffic_basis": "ncu one-layer capture scaled by params per launch",
+                "note": "update rounds overlap the BF16 all-gather, which shares SMs and HBM"}
+    if opt.peer_writes:
+        # fused update + all-gather: the slower of the HBM work and the NVLink sends bounds the launch
+        link_bytes = 2 * owned * (world - 1)
+        t_hbm = APPLY_BYTES * owned / (hbm * 1e9)
+        t_link = link_bytes / (NVLINK_GBS * 1e9)
+        roofline = {"bound": "nvlink" if t_link > t_hbm else "hbm", "kernel": "mb_adamw_apply_tiles_peers",
+                    "achieved": (max(t_hbm, t_link) / (apply_ms / 1e3)), "peak": 1.0, "unit": "of target time",
+                    "frac": max(t_hbm, t_link) / (apply_ms / 1e3),
+                    "target_ms": 1e3 * max(t_hbm, t_link), "hbm_ms": 1e3 * t_hbm, "nvlink_ms": 1e3 * t_link,
+                    "nvlink_bytes_per_rank": link_bytes, "nvlink_peak_gbs": NVLINK_GBS,
+                    "nvlink_achieved_gbs": link_bytes / (apply_ms / 1e3) / 1e9,
+                    "hbm_achieved_gbs": achieved, "hbm_peak": hbm, "peak_kind": peak_kind,
+                    "algorithmic_bytes_per_launch": APPLY_BYTES * owned,
+                    "traffic": APPLY_TRAFFIC_PER_PARAM * owned,
+                    "traffic_basis": "ncu one-layer capture scaled by params per launch (HBM side)",
+                    "note": "kernel 1 stores each BF16 copy into every rank's buffer over NVLink (peer "
+                            "pointers); target = max(HBM bytes / measured HBM peak, NVLink bytes / "
+                            "measured 770 GB/s peer copy)"}
     line = {
         "metric": METRIC, "value": total / (ms_per_step / 1e3), "unit": "params/s", "n_gpus": world,
         "steps": k, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -934,17 +959,14 @@ def run_morph_zero(args, rank, world, local_rank):
         "hbm_gbs": (APPLY_BYTES + STATS_BYTES) * total / (ms_per_step / 1e3) / 1e9,
         "phases_ms": {"stats_allreduce_finalize": stats_ms, "update_rounds": apply_ms,
                       "allgather_tail": tail_ms},
-        "roofline": {"bound": "hbm", "kernel": "mb_adamw_apply_tiles", "achieved": achieved, "peak": hbm,
-                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
-                     "algorithmic_bytes_per_launch": APPLY_BYTES * owned,
-                     "traffic": APPLY_TRAFFIC_PER_PARAM * owned,
-                     "traffic_basis": "ncu one-layer capture scaled by params per launch",
-                     "note": "update rounds overlap the BF16 all-gather, which shares SMs and HBM"},
+        "all_gather": "fused into kernel 1 (peer stores over NVLink)" if opt.peer_writes else "NCCL, per round",
+        "roofline": roofline,
         "gpu_launches": (2 + opt.rounds) * k,
         "clocks": clocks,
     }
     if e2e is not None:
         line["e2e"] = e2e
+    opt.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -1039,6 +1061,8 @@ def main():
                          "5: row-sparse AdamW on pinned-host state")
     ap.add_argument("--rounds", type=int, default=8, help="N > 1: update/all-gather rounds per step")
     ap.add_argument("--reserve-sms", type=int, default=24, help="N > 1: SMs left to NCCL during the update")
+    ap.add_argument("--no-peer-writes", action="store_true",
+                    help="N > 1: NCCL all-gather rounds instead of kernel 1's peer stores")
     ap.add_argument("--ns-shape", default=None, help="profiling only, with --config 4: one matrix, e.g. 4096x4096")
     ap.add_argument("--extra", choices=["disk", "accum", "export", "all"], default=None,
                     help="measure a path beside the configs' step instead (one GPU)")

@@ -184,6 +184,27 @@ MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* plan, int64_t tile_lo, int6
 /* mb_grad_stats (fused finalize) followed by mb_adamw_apply. */
 MB_API int mb_adamw_step(const mb_adamw_plan* plan, const mb_finalize_opts* fin, mb_stream_t stream);
 
+/* Kernel 1 over tiles [tile_lo, tile_hi) that also stores every low-precision
+ * copy into n_peers other GPUs' buffers: the value written at address a is
+ * also written at a + peer_deltas[i] (bytes; multiples of 16) for each i, where
+ * the peer buffers are mapped into this process (mb_ipc_open). This fuses the
+ * sharded step's update with its all-gather of the low-precision weights
+ * (no counterpart in the reference, which is single-process). The stores are
+ * ordered (system scope) before the kernel completes; a collective after it on
+ * every rank (e.g. a one-element all-reduce) makes them complete everywhere.
+ * Requires out_dtype != MB_NONE; n_peers <= 15. */
+MB_API int mb_adamw_apply_tiles_peers(const mb_adamw_plan* plan, int64_t tile_lo, int64_t tile_hi, int32_t max_ctas,
+                                      const int64_t* peer_deltas, int32_t n_peers, mb_stream_t stream);
+
+/* Peer-writable buffers on one node (cudaMalloc + CUDA IPC). mb_ipc_alloc
+ * allocates `bytes` on the current device and writes its 64-byte handle;
+ * another process on the node maps it with mb_ipc_open (peer access enabled)
+ * and unmaps it with mb_ipc_close before the owner calls mb_ipc_free. */
+MB_API int mb_ipc_alloc(size_t bytes, void** ptr, void* handle);
+MB_API int mb_ipc_free(void* ptr);
+MB_API int mb_ipc_open(const void* handle, void** ptr);
+MB_API int mb_ipc_close(void* ptr);
+
 /* No counterpart in the reference. mb_adamw_step for callers that cannot
  * allocate device memory (a host framework whose allocator already holds the
  * whole GPU, or a binding handed fixed buffers with no allocator of its own).

@@ -99,6 +99,11 @@ SIGNATURES = {
     "mb_accumulate_workspace_bytes": (ctypes.c_size_t, []),
     "mb_grad_accumulate": (ctypes.c_int, [_p, _p, _i32, _i64, ctypes.c_float, _i32, _p, _p, _p]),
     "mb_export_f16": (ctypes.c_int, [_p, _i64, _p, _p, _p]),
+    "mb_adamw_apply_tiles_peers": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _i32, _p]),
+    "mb_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, _p, _p]),
+    "mb_ipc_free": (ctypes.c_int, [_p]),
+    "mb_ipc_open": (ctypes.c_int, [_p, _p]),
+    "mb_ipc_close": (ctypes.c_int, [_p]),
     "mb_muon_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
     "mb_muon_batch_workspace_bytes": (ctypes.c_size_t, [_i32, _i64, _i64]),
     "mb_newton_schulz": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _i32, _p, _p, ctypes.c_size_t, _p, _p]),

@@ -61,6 +61,8 @@ int grid_for(const void* fn, int64_t n_tiles) {
 
 namespace {
 
+constexpr int kMaxPeers = 15;  // other GPUs of one node a launch can write to
+
 struct ApplyArgs {
   const mb_segment* segs;
   const mb_group* groups;
@@ -69,6 +71,11 @@ struct ApplyArgs {
   int64_t tile_lo;         // first tile of the launch
   int64_t n_tiles;         // one past the last tile of the launch
   int32_t n_segs;
+  // Peer copies (bulk kernel only): every low-precision value is also stored at
+  // the same offset of n_peers other GPUs' buffers, i.e. at out + peer_delta[p]
+  // bytes (the peers' buffers mapped into this process).
+  int32_t n_peers;
+  int64_t peer_delta[kMaxPeers];
 };
 
 __device__ __forceinline__ StepScalars group_scalars(const mb_group& g, float2 ss) {
@@ -325,8 +332,21 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkCtasPerSm) k_adamw_apply_bu
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
         // the direct path covers a tile with 256 threads x 2 quads
-        for (int part = ct; part < kThreads; part += 32 * kBulkConsumerWarps)
+        for (int part = ct; part < kThreads; part += 32 * kBulkConsumerWarps) {
           apply_tile<GDT, ODT>(seg, t, seg_vec_ok(seg, GDT, ODT), sc, prep, part);
+          if constexpr (ODT != MB_NONE) {
+            // replicate the copies this thread just wrote
+            uint16_t* o = static_cast<uint16_t*>(seg.out);
+            for (int h = 0; h < 2 && a.n_peers > 0; ++h) {
+              const int64_t q = t * kTile + part * kQuad + h * kHalf;
+              for (int64_t j = q; j < q + kQuad && j < seg.numel; ++j) {
+                const uint16_t val = o[j];
+                for (int pr = 0; pr < a.n_peers; ++pr)
+                  *reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(o + j) + a.peer_delta[pr]) = val;
+              }
+            }
+          }
+        }
         continue;
       }
       const uint8_t* base = smem + s * STAGE;
@@ -357,9 +377,14 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkCtasPerSm) k_adamw_apply_bu
         st4f(seg.w + ge, make_float4(ww[0], ww[1], ww[2], ww[3]));
         st4f(seg.m + ge, make_float4(mm[0], mm[1], mm[2], mm[3]));
         st4f(seg.v + ge, make_float4(vv[0], vv[1], vv[2], vv[3]));
-        if constexpr (ODT != MB_NONE) store4<ODT>(seg.out, ge, ww);
+        if constexpr (ODT != MB_NONE) {
+          store4<ODT>(seg.out, ge, ww);
+          for (int pr = 0; pr < a.n_peers; ++pr)
+            store4<ODT>(static_cast<char*>(seg.out) + a.peer_delta[pr], ge, ww);
+        }
       }
     }
+    if (a.n_peers > 0) __threadfence_system();  // peer stores ordered before whatever signals completion
   }
   __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) atomicExch(&st->status, MB_ERR_TIMEOUT);
@@ -835,7 +860,7 @@ MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* p, int64_t tile_lo, int64_t
   ApplyFn fn = pick_apply(p->grad_dtype, p->out_dtype);
   if (!fn) return MB_ERR_ARG;
   BulkFn bulk = pick_apply_bulk(p->grad_dtype, p->out_dtype);
-  ApplyArgs a;
+  ApplyArgs a{};
   a.segs = p->segs;
   a.groups = p->groups;
   a.seg_scal = reinterpret_cast<const float2*>(static_cast<const char*>(p->workspace) + kSegScalOffset);
@@ -854,6 +879,35 @@ MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* p, int64_t tile_lo, int64_t
   int grid = grid_for(reinterpret_cast<const void*>(fn), tile_hi - tile_lo);
   if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
   fn<<<grid, kThreads, 0, (cudaStream_t)stream>>>(a);
+  return launch_status();
+}
+
+MB_API int mb_adamw_apply_tiles_peers(const mb_adamw_plan* p, int64_t tile_lo, int64_t tile_hi, int32_t max_ctas,
+                                      const int64_t* peer_deltas, int32_t n_peers, mb_stream_t stream) {
+  int rc = check_plan(p);
+  if (rc) return rc;
+  if (tile_lo < 0 || tile_hi > p->n_tiles || tile_lo > tile_hi) return MB_ERR_ARG;
+  if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && !peer_deltas)) return MB_ERR_ARG;
+  if (n_peers > 0 && p->out_dtype == MB_NONE) return MB_ERR_ARG;
+  for (int i = 0; i < n_peers; ++i)
+    if (peer_deltas[i] % 16) return MB_ERR_ALIGN;  // keeps the copies' vector alignment
+  if (tile_lo == tile_hi) return MB_OK;
+  BulkFn bulk = pick_apply_bulk(p->grad_dtype, p->out_dtype);
+  if (!bulk.fn || !bulk_ready(bulk.fn, bulk.smem)) return MB_ERR_CUDA;
+  ApplyArgs a{};
+  a.segs = p->segs;
+  a.groups = p->groups;
+  a.seg_scal = reinterpret_cast<const float2*>(static_cast<const char*>(p->workspace) + kSegScalOffset);
+  a.state = p->state;
+  a.tile_lo = tile_lo;
+  a.n_tiles = tile_hi;
+  a.n_segs = p->n_segs;
+  a.n_peers = n_peers;
+  for (int i = 0; i < n_peers; ++i) a.peer_delta[i] = peer_deltas[i];
+  int64_t grid = (int64_t)sm_count() * kBulkCtasPerSm;
+  if (max_ctas > 0) grid = max_ctas * kBulkCtasPerSm / 3 > 0 ? max_ctas * kBulkCtasPerSm / 3 : 1;
+  if (grid > tile_hi - tile_lo) grid = tile_hi - tile_lo;
+  bulk.fn<<<(int)grid, kBulkThreads, bulk.smem, (cudaStream_t)stream>>>(a);
   return launch_status();
 }
 

@@ -62,6 +62,60 @@ def shard_pieces(sizes, lo, hi):
     return pieces
 
 
+class _CudaArray:
+    """__cuda_array_interface__ over a raw device pointer (no ownership)."""
+
+    def __init__(self, ptr, n, typestr):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3}
+
+
+class PeerBuffer:
+    """A device buffer of this rank that every rank of the group (one node) has
+    mapped: ``tensor`` is the local view, ``deltas`` the byte offsets from a
+    local address to the same element in each other rank's buffer."""
+
+    def __init__(self, nbytes, device, group=None):
+        self.device = torch.device(device)
+        self.group = group
+        lib = _lib.lib()
+        handle = (ctypes.c_uint8 * 64)()
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.mb_ipc_alloc(int(nbytes), ctypes.byref(ptr), handle), "mb_ipc_alloc")
+        self.ptr = ptr.value
+        self.nbytes = int(nbytes)
+        handles = [None] * dist.get_world_size(group)
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        me = dist.get_rank(group)
+        self.peers = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == me:
+                    continue
+                pp = ctypes.c_void_p()
+                _lib.check(lib.mb_ipc_open((ctypes.c_uint8 * 64).from_buffer_copy(h), ctypes.byref(pp)), "mb_ipc_open")
+                self.peers.append(pp.value)
+        self.deltas = [pp - self.ptr for pp in self.peers]
+        raw = torch.as_tensor(_CudaArray(self.ptr, self.nbytes // 2, "<i2"), device=self.device)
+        self.tensor = raw.view(torch.bfloat16)
+
+    def close(self):
+        """Unmap the peers' buffers, wait for every rank, free this rank's."""
+        if self.ptr is None:
+            return
+        lib = _lib.lib()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for pp in self.peers:
+                lib.mb_ipc_close(ctypes.c_void_p(pp))
+        self.peers = []
+        dist.barrier(group=self.group)  # no rank still maps this buffer
+        self.tensor = None
+        with torch.cuda.device(self.device):
+            lib.mb_ipc_free(ctypes.c_void_p(self.ptr))
+        self.ptr = None
+
+
 class CudaZeroBackend:
     """Kernel calls of one ZeRO step on the rank's GPU (C-ABI library)."""
 
@@ -106,11 +160,19 @@ class CudaZeroBackend:
                                                         _lib.stream_handle()), "mb_step_finalize")
         self.engine.max_clock += 1
 
-    def apply_round(self, k):
+    def apply_round(self, k, peer_deltas=None):
+        """Kernel 1 on round k's tiles; with ``peer_deltas`` every low-precision
+        value is also stored into the other ranks' buffers (fused all-gather)."""
         lo, hi = self._round_tiles[k], self._round_tiles[k + 1]
         with torch.cuda.device(self.device):
-            _lib.check(self.engine.lib.mb_adamw_apply_tiles(ctypes.byref(self._plan), lo, hi, self.max_ctas,
-                                                            _lib.stream_handle()), "mb_adamw_apply_tiles")
+            if peer_deltas:
+                arr = (ctypes.c_int64 * len(peer_deltas))(*peer_deltas)
+                _lib.check(self.engine.lib.mb_adamw_apply_tiles_peers(
+                    ctypes.byref(self._plan), lo, hi, 0, arr, len(peer_deltas), _lib.stream_handle()),
+                    "mb_adamw_apply_tiles_peers")
+            else:
+                _lib.check(self.engine.lib.mb_adamw_apply_tiles(ctypes.byref(self._plan), lo, hi, self.max_ctas,
+                                                                _lib.stream_handle()), "mb_adamw_apply_tiles")
 
     def last_step(self) -> dict:
         st = self.engine.read_state()
@@ -130,7 +192,7 @@ class ZeroAdamW:
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-2, *, max_norm=None,
                  clip_mode="torch", gate=False, low_precision=torch.bfloat16, process_group=None, device=None,
-                 backend=None, rounds=8, reserve_sms=24):
+                 backend=None, rounds=8, reserve_sms=24, peer_writes="auto"):
         params = list(params)
         if not params:
             raise ValueError("ZeroAdamW needs parameters")
@@ -146,7 +208,9 @@ class ZeroAdamW:
         self.shapes = [tuple(p.shape) for p in params]
         self.sizes = [p.numel() for p in params]
         self.total = sum(self.sizes)
-        self.rounds = 1 if self.world == 1 else max(1, int(rounds))
+        self.peer_writes = self._want_peers(peer_writes, backend)
+        # peer writes replace the per-round all-gathers: one update launch stores everywhere
+        self.rounds = 1 if self.world == 1 or self.peer_writes else max(1, int(rounds))
         self.cs = chunk_size(self.total, self.world, self.rounds)
         self.chunks = rank_chunks(self.total, self.world, self.rank, self.rounds, self.cs)
         # pieces: (tensor index, offset in tensor, offset in the masters, length, round)
@@ -160,7 +224,15 @@ class ZeroAdamW:
             self.master[s_off:s_off + n].copy_(src.to(self.device, torch.float32))
         self.exp_avg = torch.zeros_like(self.master)
         self.exp_avg_sq = torch.zeros_like(self.master)
-        self.flat_weights = torch.zeros(self.rounds * self.world * self.cs, dtype=low_precision, device=self.device)
+        self._peer = None
+        n_flat = self.rounds * self.world * self.cs
+        if self.peer_writes:
+            self._peer = PeerBuffer(2 * n_flat + 16, self.device, process_group)
+            self.flat_weights = self._peer.tensor.view(torch.int16)[:n_flat].view(low_precision)
+            self.flat_weights.zero_()
+            self._done = torch.zeros(1, dtype=torch.float32, device=self.device)
+        else:
+            self.flat_weights = torch.zeros(n_flat, dtype=low_precision, device=self.device)
         off = 0
         self.weights = []
         for shape, n in zip(self.shapes, self.sizes):
@@ -174,6 +246,30 @@ class ZeroAdamW:
         self.backend = (backend if backend is not None else
                         CudaZeroBackend(self.device, reserve_sms if self.world > 1 else 0))
         self._keys = [object() for _ in self.pieces]  # one clock slot per piece
+
+    def _want_peers(self, peer_writes, backend):
+        """Fused update + all-gather (kernel 1 stores the low-precision copies
+        into every rank's buffer over NVLink) when the ranks share a node."""
+        if self.world == 1 or backend is not None or self.low_precision not in (torch.bfloat16, torch.float16):
+            if peer_writes is True:
+                raise ValueError("peer writes need several ranks, the CUDA backend and a 16-bit copy")
+            return False
+        if peer_writes in (True, False):
+            return peer_writes
+        if peer_writes != "auto":
+            raise ValueError("peer_writes must be True, False or 'auto'")
+        import socket
+        hosts = [None] * self.world
+        dist.all_gather_object(hosts, socket.gethostname(), group=self.group)
+        return len(set(hosts)) == 1 and self.world - 1 <= 15
+
+    def close(self):
+        """Release the peer-mapped buffer (collective: every rank calls it)."""
+        if self._peer is not None:
+            self.flat_weights = self.flat_weights.clone()
+            self.weights = [w.clone() for w in self.weights]
+            self._peer.close()
+            self._peer = None
 
     def _own(self, k):
         base = (k * self.world + self.rank) * self.cs
@@ -228,15 +324,19 @@ class ZeroAdamW:
         if events:
             events[1].record()
         works = []
+        deltas = self._peer.deltas if self._peer is not None else None
         for k in range(self.rounds):
             if entries:
-                self.backend.apply_round(k)
-            if self.world > 1:
+                self.backend.apply_round(k, deltas) if deltas else self.backend.apply_round(k)
+            if self.world > 1 and deltas is None:
                 works.append(self._gather(k))
         if events:
             events[2].record()
         for w in works:
             w.wait()
+        if deltas is not None:
+            # every rank's stores into every buffer are complete once all ranks pass this
+            dist.all_reduce(self._done, group=self.group)
         if events:
             events[3].record()
         if self.gate:

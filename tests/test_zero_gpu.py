@@ -23,10 +23,11 @@ def _inputs():
     return params, grads
 
 
-def _run(device):
+def _run(device, peer_writes="auto"):
     from morph_b200.zero import ZeroAdamW
     params, grads = _inputs()
-    opt = ZeroAdamW([p.to(device) for p in params], LR, BETAS, EPS, WD, max_norm=1.0, gate=True, device=device)
+    opt = ZeroAdamW([p.to(device) for p in params], LR, BETAS, EPS, WD, max_norm=1.0, gate=True, device=device,
+                    peer_writes=peer_writes)
     coefs = []
     for gs in grads:
         opt.step([g.to(device) for g in gs])
@@ -35,10 +36,12 @@ def _run(device):
     flat = torch.full((total,), float("nan"))
     for k, lo, hi in opt.chunks:
         flat[lo:hi] = opt.master[k * opt.cs:k * opt.cs + hi - lo].cpu()
-    return (flat, opt.flat_weights[:total].cpu(), coefs)
+    out = (flat, opt.flat_weights[:total].cpu(), coefs, opt.peer_writes)
+    opt.close()
+    return out
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, peer_writes="auto"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -46,12 +49,15 @@ def _worker(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        q.put((rank, _run(torch.device("cuda", rank))))
+        q.put((rank, _run(torch.device("cuda", rank), peer_writes)))
     finally:
         dist.destroy_process_group()
 
 
-def test_zero_two_gpus_equal_one_gpu(cuda):
+@pytest.mark.parametrize("peer_writes", [True, False])
+def test_zero_two_gpus_equal_one_gpu(cuda, peer_writes):
+    """peer_writes=True: kernel 1 stores the BF16 copies into both GPUs' buffers
+    (fused all-gather); False: NCCL all-gather rounds. Both equal one GPU."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     with socket.socket() as s:
@@ -59,15 +65,16 @@ def test_zero_two_gpus_equal_one_gpu(cuda):
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, peer_writes)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=180) for _ in procs)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    flat0, full0, c0 = results[0]
-    flat1, full1, c1 = results[1]
+    flat0, full0, c0, p0 = results[0]
+    flat1, full1, c1, p1 = results[1]
+    assert p0 == p1 == peer_writes
     assert c0 == c1
     masters = torch.where(torch.isnan(flat0), flat1, flat0)
     assert not torch.isnan(masters).any()
