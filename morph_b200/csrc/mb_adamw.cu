@@ -547,9 +547,12 @@ __device__ __forceinline__ void stats_elems(const uint4& q, bool unscale, const 
   }
 }
 
+#ifndef MB_STATS_U
+#define MB_STATS_U 4
+#endif
 template <int GDT, bool UNSCALE>
 __global__ void __launch_bounds__(kThreads) k_grad_stats(StatsArgs a) {
-  constexpr int kU = 4;                                  // tiles in flight per iteration
+  constexpr int kU = MB_STATS_U;                         // tiles in flight per iteration
   constexpr int kEpl = GDT == MB_F32 ? 4 : 8;            // elements per 16-byte load
   constexpr int kLoads = (kTile / kThreads) / kEpl;      // 16-byte loads per thread per tile
   using T = typename Elem<GDT>::T;
