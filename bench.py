@@ -386,16 +386,18 @@ def run_ns_only(args):
                       "tflops_executed": ns_flops_executed(rows, cols) / (ms / 1e3) / 1e12}), flush=True)
 
 
-def config4_model(device):
+def config4_model(device, layers=32):
     """Config 4's parameters (random init) with seeded BF16 gradients N(0, 1e-4):
     32 layers x {3 x [4096, 11008], 4 x [4096, 4096]} Linear weights, a
     [65536, 4096] embedding and 64 vectors [4096]. Every rank builds the same."""
+
+    n_layers = layers
 
     class Model(torch.nn.Module):
         def __init__(self):
             super().__init__()
             layers = []
-            for _ in range(32):
+            for _ in range(n_layers):
                 layers += [torch.nn.Linear(11008, 4096, bias=False, device=device) for _ in range(3)]
                 layers += [torch.nn.Linear(4096, 4096, bias=False, device=device) for _ in range(4)]
             self.layers = torch.nn.ModuleList(layers)
@@ -415,6 +417,12 @@ def config4_model(device):
 CONFIG4_WORKLOAD = ("config4: Muon 32 x {3 x [4096,11008], 4 x [4096,4096]} + AdamW [65536,4096] + 64 x [4096]")
 
 
+def config4_workload(args):
+    if args.c4_layers == 32:
+        return CONFIG4_WORKLOAD
+    return f"config4 reduced for profiling: {args.c4_layers} layers"
+
+
 def run_config4_zero(args, rank, world, local_rank):
     """Config 4 on N GPUs: ZeroHybridMuonAdamW (whole Muon matrices dealt over
     the ranks, AdamW group flat-sharded, BF16 weights all-gathered per round).
@@ -422,7 +430,7 @@ def run_config4_zero(args, rank, world, local_rank):
     import torch.distributed as dist
     from morph_b200.zero import ZeroHybridMuonAdamW
     device = torch.device("cuda", local_rank)
-    model = config4_model(device)
+    model = config4_model(device, args.c4_layers)
     opt = ZeroHybridMuonAdamW(model, lr=3e-4, weight_decay=.1, ns_dtype="bf16", device=device)
     grads = [p.grad for p in model.parameters()]
     for _ in range(args.warmup):
@@ -455,7 +463,7 @@ def run_config4_zero(args, rank, world, local_rank):
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
                 "higher_is_better": False, "scaling": "strong", "dtype": "bf16 NS operands, f32 state",
                 "data": "synthetic",
-                "config": {"workload": CONFIG4_WORKLOAD, "parallelism": f"muon-matrix-shard + zero1-dp{world}",
+                "config": {"workload": config4_workload(args), "parallelism": f"muon-matrix-shard + zero1-dp{world}",
                            "muon_matrices_per_rank": len(opt.owned), "rounds": len(opt.rounds)},
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak * world,
                              "peak_kind": "measured sustained x n_gpus" if peaks else "fallback x n_gpus",
@@ -477,7 +485,7 @@ def run_config4(args):
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
 
-    model = config4_model(device)
+    model = config4_model(device, args.c4_layers)
     opt = HybridMuonAdamW(model, lr=3e-4, weight_decay=.1, ns_dtype="bf16")
     muon_params = sum(p.numel() for p in opt.muon)
     adam_params = sum(p.numel() for g in opt.adam.param_groups for p in g["params"])
@@ -543,7 +551,7 @@ def run_config4(args):
     line = {"metric": "Hybrid Muon+AdamW step (config 4, 7B shape)", "value": step_ms / 1e3, "unit": "s/step",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
             "higher_is_better": False, "dtype": "bf16 NS operands, f32 state", "data": "synthetic",
-            "config": {"workload": CONFIG4_WORKLOAD, "muon_params": muon_params,
+            "config": {"workload": config4_workload(args), "muon_params": muon_params,
                        "adam_params": adam_params, "ns_flop_per_step": total_flop},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "peak_kind": "measured sustained" if peaks else "fallback", "unit": "TFLOP/s",
@@ -1095,6 +1103,7 @@ def main():
     ap.add_argument("--reserve-sms", type=int, default=24, help="N > 1: SMs left to NCCL during the update")
     ap.add_argument("--no-peer-writes", action="store_true",
                     help="N > 1: NCCL all-gather rounds instead of kernel 1's peer stores")
+    ap.add_argument("--c4-layers", type=int, default=32, help="profiling only: fewer layers than config 4")
     ap.add_argument("--ns-shape", default=None, help="profiling only, with --config 4: one matrix, e.g. 4096x4096")
     ap.add_argument("--extra", choices=["disk", "accum", "export", "all"], default=None,
                     help="measure a path beside the configs' step instead (one GPU)")
