@@ -15,6 +15,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+from _mp import from_host, to_host
+
 from morph_b200.zero import ZeroAdamW, chunk_size, rank_chunks, shard_pieces
 
 SHAPES = [(37,), (100, 3), (64, 64), (5,), (1000,)]
@@ -99,7 +101,7 @@ def _worker(rank, world, port, q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        q.put((rank, _run(world, rank)))
+        q.put((rank, to_host(_run(world, rank))))
     finally:
         dist.destroy_process_group()
 
@@ -135,7 +137,7 @@ def test_two_gloo_ranks_equal_one_rank():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=120) for _ in procs)
+    results = {r: from_host(v) for r, v in (q.get(timeout=120) for _ in procs)}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

@@ -10,6 +10,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+from _mp import from_host, to_host
+
 pytestmark = pytest.mark.gpu
 
 SHAPES = [(37,), (3072, 300), (4096, 64), (5,), (100000,)]
@@ -49,7 +51,7 @@ def _worker(rank, world, port, q, peer_writes="auto"):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        q.put((rank, _run(torch.device("cuda", rank), peer_writes)))
+        q.put((rank, to_host(_run(torch.device("cuda", rank), peer_writes))))
     finally:
         dist.destroy_process_group()
 
@@ -68,7 +70,7 @@ def test_zero_two_gpus_equal_one_gpu(cuda, peer_writes):
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q, peer_writes)) for r in range(2)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=180) for _ in procs)
+    results = {r: from_host(v) for r, v in (q.get(timeout=180) for _ in procs)}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

@@ -15,6 +15,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+from _mp import from_host, to_host
+
 from morph_b200.zero import ZeroHybridMuonAdamW, deal_matrices
 from test_zero_cpu import OracleBackend
 
@@ -89,7 +91,7 @@ def _worker(rank, world, port, q, poison):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        q.put((rank, _run(poison)))
+        q.put((rank, to_host(_run(poison))))
     finally:
         dist.destroy_process_group()
 
@@ -107,7 +109,7 @@ def _two_ranks(poison=None):
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q, poison)) for r in range(2)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=180) for _ in procs)
+    results = {r: from_host(v) for r, v in (q.get(timeout=180) for _ in procs)}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

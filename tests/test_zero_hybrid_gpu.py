@@ -11,6 +11,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+from _mp import from_host, to_host
+
 pytestmark = pytest.mark.gpu
 
 LR, WD = .02, .01
@@ -69,7 +71,7 @@ def _worker(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        q.put((rank, _run_zero(torch.device("cuda", rank))))
+        q.put((rank, to_host(_run_zero(torch.device("cuda", rank)))))
     finally:
         dist.destroy_process_group()
 
@@ -85,7 +87,7 @@ def test_two_gpus_equal_one_gpu(cuda):
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=180) for _ in procs)
+    results = {r: from_host(v) for r, v in (q.get(timeout=180) for _ in procs)}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
