@@ -25,11 +25,11 @@ def _inputs():
     return params, grads
 
 
-def _run(device, peer_writes="auto"):
+def _run(device, peer_writes="auto", low=torch.bfloat16):
     from morph_b200.zero import ZeroAdamW
     params, grads = _inputs()
     opt = ZeroAdamW([p.to(device) for p in params], LR, BETAS, EPS, WD, max_norm=1.0, gate=True, device=device,
-                    peer_writes=peer_writes)
+                    peer_writes=peer_writes, low_precision=low)
     coefs = []
     for gs in grads:
         opt.step([g.to(device) for g in gs])
@@ -43,7 +43,7 @@ def _run(device, peer_writes="auto"):
     return out
 
 
-def _worker(rank, world, port, q, peer_writes="auto"):
+def _worker(rank, world, port, q, peer_writes="auto", low=torch.bfloat16):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -51,13 +51,14 @@ def _worker(rank, world, port, q, peer_writes="auto"):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        q.put((rank, to_host(_run(torch.device("cuda", rank), peer_writes))))
+        q.put((rank, to_host(_run(torch.device("cuda", rank), peer_writes, low))))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("peer_writes", [True, False])
-def test_zero_two_gpus_equal_one_gpu(cuda, peer_writes):
+@pytest.mark.parametrize("peer_writes,low", [(True, torch.bfloat16), (False, torch.bfloat16),
+                                             (True, torch.float16)])
+def test_zero_two_gpus_equal_one_gpu(cuda, peer_writes, low):
     """peer_writes=True: kernel 1 stores the BF16 copies into both GPUs' buffers
     (fused all-gather); False: NCCL all-gather rounds. Both equal one GPU."""
     if torch.cuda.device_count() < 2:
@@ -67,7 +68,7 @@ def test_zero_two_gpus_equal_one_gpu(cuda, peer_writes):
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, peer_writes)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, peer_writes, low)) for r in range(2)]
     for p in procs:
         p.start()
     results = {r: from_host(v) for r, v in (q.get(timeout=180) for _ in procs)}
@@ -80,7 +81,7 @@ def test_zero_two_gpus_equal_one_gpu(cuda, peer_writes):
     assert c0 == c1
     masters = torch.where(torch.isnan(flat0), flat1, flat0)
     assert not torch.isnan(masters).any()
-    single = _run(cuda)
+    single = _run(cuda, low=low)
     torch.testing.assert_close(masters, single[0], rtol=1e-6, atol=1e-6 * LR)
     assert torch.equal(full0, full1)
     torch.testing.assert_close(full0.float(), single[1].float(), rtol=1e-2, atol=0)
