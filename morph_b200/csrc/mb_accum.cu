@@ -47,28 +47,29 @@ __global__ void __launch_bounds__(kThreads) k_accumulate(float* __restrict__ acc
       }
     }
   }
-  if (!STATS) return;
-  __shared__ double red[kThreads / 32];
-  __shared__ bool last;
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_down_sync(0xffffffffu, ss, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double b = 0.0;
-    for (int i = 0; i < kThreads / 32; ++i) b += red[i];
-    partials[blockIdx.x] = b;
-    __threadfence();
-    last = atomicAdd(ticket, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (last && threadIdx.x == 0) {
-    __threadfence();
-    double t = 0.0;
-    for (unsigned i = 0; i < gridDim.x; ++i) t += __ldcg(&partials[i]);
-    // squares are >= 0, so the sum is finite exactly when every element is
-    record[0] += t;
-    record[1] += isfinite(t) ? 0.0 : 1.0;
-    *ticket = 0u;
+  if constexpr (STATS) {
+    __shared__ double red[kThreads / 32];
+    __shared__ bool last;
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_down_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double b = 0.0;
+      for (int i = 0; i < kThreads / 32; ++i) b += red[i];
+      partials[blockIdx.x] = b;
+      __threadfence();
+      last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+      __threadfence();
+      double t = 0.0;
+      for (unsigned i = 0; i < gridDim.x; ++i) t += __ldcg(&partials[i]);
+      // squares are >= 0, so the sum is finite exactly when every element is
+      record[0] += t;
+      record[1] += isfinite(t) ? 0.0 : 1.0;
+      *ticket = 0u;
+    }
   }
 }
 

@@ -42,7 +42,6 @@ struct Layout {
   int batch;
   int64_t mp, np;
   size_t partials, tickets, divisors, x, t0, t1, a, b, o, total;
-  size_t stats_bytes() const { return x - partials; }
 };
 
 // Workspace: [FP64 partials][tickets][divisors][X][XT0][XT1][A][B][O f32 (optional)],
