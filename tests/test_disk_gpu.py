@@ -117,3 +117,24 @@ def test_cast_and_fp16_export_check(cuda):
         cast_f32(bad, torch.float16, export_check=True)
     edge = torch.tensor([65504.0, -65504.0], device=cuda)
     assert cast_f32(edge, torch.float16, export_check=True).tolist() == [65504.0, -65504.0]
+
+
+def test_disk_update_step_gap_and_clips_bit_exact(cuda):
+    """tests/test_state_cache.py:34-46 of the reference: clips .25 / 1 / .1 and a
+    step gap (clocks 1, 2, 5); every plane bit-exact with the oracle."""
+    from morph_b200.disk import DeviceDiskState
+    r = orc.rng(31)
+    n = 10_001
+    w0 = r.standard_normal(n).astype(np.float32) * np.float32(.02)
+    planes = torch.zeros(3, n, device=cuda)
+    planes[0] = torch.from_numpy(w0).to(cuda)
+    store = DeviceDiskState({"p": planes})
+    w, m, v = w0.copy(), np.zeros(n, np.float32), np.zeros(n, np.float32)
+    for step, clip in ((1, .25), (2, 1.0), (5, .1)):
+        g = r.standard_normal(n).astype(np.float32) * np.float32(1e-2)
+        store.update("p", torch.from_numpy(g).to(cuda), step, 1e-3, clip)
+        orc.adamw_(w, m, v, orc.grad_prepare(g, coef=clip), orc.disk_scalars(1e-3, step))
+    got = planes.cpu().numpy()
+    np.testing.assert_array_equal(got[0], w)
+    np.testing.assert_array_equal(got[1], m)
+    np.testing.assert_array_equal(got[2], v)

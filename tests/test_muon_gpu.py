@@ -269,3 +269,43 @@ def test_hybrid_batches_by_shape_match_one_matrix_batches(cuda):
     for p, q in zip(opts[0].muon, opts[1].muon):
         assert torch.equal(opts[0].low_precision_copies[p], opts[1].low_precision_copies[q])
         assert torch.equal(opts[0].low_precision_copies[p], p.detach().bfloat16())
+
+
+def test_adam_group_matches_torch_adamw_bit_exactly(cuda):
+    """tests/test_training.py:9-27 of the reference: the AdamW group inside the
+    hybrid equals a standalone torch.optim.AdamW(betas=(.9, .95), wd=.01,
+    foreach=False) bit for bit over 3 steps of constant gradients .2, and a NaN
+    gradient raises FloatingPointError leaving the model bit-identical."""
+    import copy
+    from morph_b200 import HybridMuonAdamW, partition
+
+    class Tiny(torch.nn.Module):  # the reference's MorphModel shapes at d_model 8
+        def __init__(self):
+            super().__init__()
+            self.embedding = torch.nn.Embedding(16, 8)
+            self.mix = torch.nn.Linear(8, 16)
+            self.out = torch.nn.Linear(16, 8)
+            self.norm = torch.nn.LayerNorm(8)
+
+    torch.manual_seed(0)
+    model = Tiny().to(cuda)
+    _, auxiliary = partition(model)
+    reference = [torch.nn.Parameter(p.detach().cpu().clone()) for p in auxiliary]
+    hybrid = HybridMuonAdamW(model, lr=.003)
+    adam = torch.optim.AdamW(reference, lr=.003, weight_decay=.01, betas=(.9, .95), foreach=False)
+    for p in model.parameters():
+        p.grad = torch.ones_like(p) * .2
+    for _ in range(3):
+        for p, q in zip(auxiliary, reference):
+            p.grad = torch.ones_like(p) * .2
+            q.grad = p.grad.cpu().clone()
+        hybrid.step()
+        adam.step()
+    for p, q in zip(auxiliary, reference):
+        torch.testing.assert_close(p.detach().cpu(), q.detach(), rtol=0, atol=0)
+    before = copy.deepcopy(model.state_dict())
+    next(model.parameters()).grad.fill_(float('nan'))
+    with pytest.raises(FloatingPointError):
+        hybrid.step()
+    for key, value in model.state_dict().items():
+        torch.testing.assert_close(value, before[key], rtol=0, atol=0)
