@@ -58,3 +58,24 @@ def test_status_codes_map_to_reference_exceptions():
         _lib.check(_lib.MB_ERR_INDEX)
     with pytest.raises(RuntimeError):
         _lib.check(_lib.MB_ERR_CUDA)
+
+
+def test_c_caller_links_and_runs(tmp_path):
+    """A plain C program including the header and linking the library (no
+    Python in the loop) runs the host-only entry points and argument checks."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    here = os.path.dirname(os.path.abspath(__file__))
+    repo = os.path.dirname(here)
+    libdir = os.path.join(repo, "morph_b200")
+    exe = tmp_path / "abi_host"
+    cuda_lib = "/usr/local/cuda/lib64"
+    cmd = [gcc, "-std=c11", "-Wall", "-Werror", os.path.join(here, "c", "abi_host.c"), "-I", os.path.join(repo, "include"),
+           "-L", libdir, "-lmorph_b200", f"-Wl,-rpath,{libdir}", f"-Wl,-rpath,{cuda_lib}", "-o", str(exe)]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert "c abi ok" in r.stdout
