@@ -73,23 +73,28 @@ class BiasCorrectionTables:
             return math.inf
         return math.ceil(60 * math.log(2) / -math.log(beta)) + 2
 
+    # longest table built (entries per row); clocks past it use its last entry,
+    # which is exact once both corrections have reached 1.0 (beta2 <= 0.99998)
+    MAX_LENGTH = 1 << 20
+
     def ensure(self, max_clock: int):
+        """The table for every registered (beta1, beta2, rule), long enough for
+        clocks up to ``max_clock``. It is built to saturation up front (bounded by
+        MAX_LENGTH), so later steps never rebuild it: a captured CUDA graph can
+        replay the step for any number of steps."""
         sat = max(max(self._saturation(b1), self._saturation(b2)) for b1, b2, _ in self.keys)
         need = max_clock + 2
-        if self.tensor is not None and (need <= self.length or self.length >= sat):
+        if self.tensor is not None and (need <= self.length or self.length >= min(sat, self.MAX_LENGTH)):
             return self.tensor, self.length
-        length = max(1024, 2 * need)
-        if sat < length:
-            length = int(sat)
+        length = int(min(max(sat, need, 2), self.MAX_LENGTH))
         rows = []
         for b1, b2, kind in self.keys:
             t1 = np.ones(length, np.float64)
             t2 = np.ones(length, np.float64)
-            for t in range(1, length):
-                ft = float(t)
-                t1[t] = 1 - b1 ** ft
-                b = 1 - b2 ** ft
-                t2[t] = b ** 0.5 if kind == "torch" else math.sqrt(b)
+            t = np.arange(1, length, dtype=np.float64)
+            t1[1:] = [1 - b1 ** ft for ft in t.tolist()]
+            bb = [1 - b2 ** ft for ft in t.tolist()]
+            t2[1:] = [x ** 0.5 for x in bb] if kind == "torch" else [math.sqrt(x) for x in bb]
             rows += [t1, t2]
         self.tensor = torch.from_numpy(np.stack(rows)).to(self.device)
         self.length = length
@@ -241,7 +246,13 @@ class AdamW(torch.optim.Optimizer):
     """torch.optim.AdamW on the B200 kernels (decoupled weight decay, no amsgrad).
 
     Parameters must be contiguous FP32 CUDA tensors on one device; gradients
-    contiguous FP32/FP16/BF16 of the parameter's shape, one dtype per step."""
+    contiguous FP32/FP16/BF16 of the parameter's shape, one dtype per step.
+
+    With ``sync=False`` (the default unless ``gate``) ``step`` only enqueues
+    kernels: clocks, the skip decision, the loss scale and the clip coefficient
+    all live on the device. After one eager step it can be captured in a CUDA
+    graph and replayed for any number of steps, provided the gradients stay at
+    the same addresses (as for torch's capturable optimizers)."""
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-2, amsgrad=False, *,
                  maximize=False, foreach=None, capturable=False, differentiable=False, fused=None,

@@ -154,3 +154,52 @@ def test_checkpoint_mid_training_continues_bit_for_bit(cuda):
         assert torch.equal(pa, pb)
         assert torch.equal(oa.state[pa]["exp_avg_sq"], ob.state[pb]["exp_avg_sq"])
         assert int(float(oa.state[pa]["step"])) == int(float(ob.state[pb]["step"])) == 5
+
+
+def test_step_captured_in_a_cuda_graph_replays_like_eager_steps(cuda):
+    """AdamW.step (sync=False) launches kernels only: captured once in a CUDA
+    graph it replays as many steps as wanted (device clocks, clip and copies
+    advance on the device), bit-identical to eager steps."""
+    from morph_b200 import AdamW
+    shapes = [(300, 7), (4099,), (64, 64)]
+    a = _params(cuda, shapes, 21)
+    b = _params(cuda, shapes, 21)
+    kw = dict(lr=1e-3, betas=(.9, .95), weight_decay=.1, max_norm=1.0, low_precision=torch.bfloat16)
+    oa, ob = AdamW(a, **kw), AdamW(b, **kw)
+    grads = [torch.zeros(s, device=cuda, dtype=torch.bfloat16) for s in shapes]  # static grad buffers
+    for p, g in zip(a, grads):
+        p.grad = g
+    gen = torch.Generator(device=cuda).manual_seed(22)
+
+    def fresh():
+        return [(torch.randn(s, device=cuda, generator=gen) * .3).to(torch.bfloat16) for s in shapes]
+
+    def eager_b(gs):
+        for p, g in zip(b, gs):
+            p.grad = g.clone()
+        ob.step()
+
+    gs = fresh()  # step 1 eager on both (builds the state and the launch plan)
+    for buf, g in zip(grads, gs):
+        buf.copy_(g)
+    oa.step()
+    eager_b(gs)
+    side = torch.cuda.Stream(cuda)
+    side.wait_stream(torch.cuda.current_stream(cuda))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+        oa.step()
+    torch.cuda.current_stream(cuda).wait_stream(side)
+    for _ in range(4):
+        gs = fresh()
+        for buf, g in zip(grads, gs):
+            buf.copy_(g)
+        graph.replay()
+        eager_b(gs)
+    torch.cuda.synchronize(cuda)
+    for pa, pb in zip(a, b):
+        assert torch.equal(pa, pb)
+        assert torch.equal(oa.state[pa]["exp_avg_sq"], ob.state[pb]["exp_avg_sq"])
+        assert torch.equal(oa.low_precision_copies[pa], ob.low_precision_copies[pb])
+        assert int(float(oa.state[pa]["step"])) == int(float(ob.state[pb]["step"])) == 5
+    assert oa.last_step()["clip_coef"] == ob.last_step()["clip_coef"] < 1.0
