@@ -173,3 +173,24 @@ def install(store, device="cuda", window_elements: int = 1 << 24) -> GpuDiskUpda
     updater = GpuDiskUpdater(store, device, window_elements)
     store.update = updater.update
     return updater
+
+
+def patch_class(cls, device="cuda", window_elements: int = 1 << 24):
+    """Route ``cls.update`` (a DiskState-like class: instances have ``root``,
+    ``entries`` and ``fault``) through one GpuDiskUpdater per instance, created
+    on first use. For engines that build their store internally (e.g.
+    streamtrain/delta_cycle.py:130-156), call this once before they run.
+    Returns a function that restores the original method."""
+    original = cls.update
+
+    def update(self, name, gradient, step, lr, clip, chunk_elements=1048576):
+        updater = self.__dict__.get("_mb_gpu_updater")
+        if updater is None:
+            updater = self.__dict__["_mb_gpu_updater"] = GpuDiskUpdater(self, device, window_elements)
+        return updater.update(name, gradient, step, lr, clip, chunk_elements)
+
+    cls.update = update
+
+    def restore():
+        cls.update = original
+    return restore

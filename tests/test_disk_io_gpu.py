@@ -94,3 +94,28 @@ def test_two_steps_two_entries(cuda, tmp_path):
     torch.cuda.synchronize()
     for name in arrays:
         np.testing.assert_array_equal(store.planes(name), ref[name])
+
+
+def test_patch_class_routes_every_instance(cuda, tmp_path):
+    """patch_class swaps a store class's update for the GPU one (one updater per
+    instance) and restores it."""
+    from morph_b200.disk_io import patch_class
+
+    class Store(FileStore):
+        def update(self, *args, **kwargs):
+            raise AssertionError("the original update must not run while patched")
+
+    n = 3000
+    planes = _planes(n, 41)
+    s1 = Store(tmp_path, {"a": planes})
+    restore = patch_class(Store, cuda, window_elements=1024)
+    try:
+        g = torch.from_numpy(orc.rng(42).standard_normal(n).astype(np.float32))
+        s1.update("a", g, 1, 1e-3, .5, chunk_elements=1000)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(s1.planes("a"), _oracle(planes, g.numpy(), 1, 1e-3, .5))
+        assert s1.calls == 3
+    finally:
+        restore()
+    with pytest.raises(AssertionError):
+        s1.update("a", g, 2, 1e-3, .5)
