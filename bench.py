@@ -449,6 +449,7 @@ def run_config4_zero(args, rank, world, local_rank):
     t = torch.tensor([start.elapsed_time(stop) / args.steps], device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms = float(t.item())
+    opt.close()
     total_flop = sum(ns_flops(*q.shape) for q in opt.muon)
     peaks = {}
     try:

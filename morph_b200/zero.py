@@ -88,13 +88,21 @@ class PeerBuffer:
         dist.all_gather_object(handles, bytes(handle), group=group)
         me = dist.get_rank(group)
         self.peers = []
-        with torch.cuda.device(self.device):
-            for r, h in enumerate(handles):
-                if r == me:
-                    continue
-                pp = ctypes.c_void_p()
-                _lib.check(lib.mb_ipc_open((ctypes.c_uint8 * 64).from_buffer_copy(h), ctypes.byref(pp)), "mb_ipc_open")
-                self.peers.append(pp.value)
+        try:
+            with torch.cuda.device(self.device):
+                for r, h in enumerate(handles):
+                    if r == me:
+                        continue
+                    pp = ctypes.c_void_p()
+                    _lib.check(lib.mb_ipc_open((ctypes.c_uint8 * 64).from_buffer_copy(h), ctypes.byref(pp)),
+                               "mb_ipc_open")
+                    self.peers.append(pp.value)
+        except Exception:
+            with torch.cuda.device(self.device):
+                for pp in self.peers:
+                    lib.mb_ipc_close(ctypes.c_void_p(pp))
+                lib.mb_ipc_free(ctypes.c_void_p(self.ptr))
+            raise
         self.deltas = [pp - self.ptr for pp in self.peers]
         raw = torch.as_tensor(_CudaArray(self.ptr, self.nbytes // 2, "<i2"), device=self.device)
         self.tensor = raw.view(torch.bfloat16)
@@ -264,7 +272,9 @@ class ZeroAdamW:
         return len(set(hosts)) == 1 and self.world - 1 <= 15
 
     def close(self):
-        """Release the peer-mapped buffer (collective: every rank calls it)."""
+        """Release the peer-mapped buffer (collective: every rank calls it).
+        ``flat_weights`` and ``weights`` become private copies; views taken from
+        them before the call are invalid afterwards."""
         if self._peer is not None:
             self.flat_weights = self.flat_weights.clone()
             self.weights = [w.clone() for w in self.weights]
@@ -559,6 +569,15 @@ class ZeroHybridMuonAdamW:
             self.adam.step(adam_grads)
         for w in works:
             w.wait()
+
+    def close(self):
+        """Release the AdamW group's peer-mapped buffer (collective)."""
+        if self.adam is not None:
+            self.adam.close()
+            aindex = {id(p): i for i, p in enumerate(self.adam_params)}
+            mindex = {id(p): i for i, p in enumerate(self.muon)}
+            self.weights = [self.muon_weights[mindex[id(p)]] if id(p) in mindex else self.adam.weights[aindex[id(p)]]
+                            for p in self.params]
 
     def state_dict(self) -> dict:
         """This rank's share: Muon masters and momentum by Muon index, the AdamW shard."""

@@ -41,8 +41,10 @@ def _run_zero(device):
     for gs in _grads(model, device):
         opt.step(gs)
     torch.cuda.synchronize(device)
-    return ({i: t.cpu() for i, t in opt.master.items()}, [w.cpu() for w in opt.weights],
-            {i: t.cpu() for i, t in opt.momentum.items()})
+    out = ({i: t.cpu() for i, t in opt.master.items()}, [w.cpu() for w in opt.weights],
+           {i: t.cpu() for i, t in opt.momentum.items()})
+    opt.close()
+    return out
 
 
 def test_one_gpu_equals_hybrid(cuda):
