@@ -142,6 +142,41 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
+def reference_muon_cpu_time(shape, seed=0):
+    """Seconds of one Muon matrix step of the reference on the host cores:
+    streamtrain/optimizer.py:52-61 with orthogonalize (optimizer.py:13-22) in
+    FP32 torch on the CPU, restated here (the reference tree is not read at run
+    time). One warm-up, one timed step."""
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(seed)
+    p = torch.randn(shape, generator=g) * .02
+    mom = torch.zeros(shape)
+    grad = (torch.randn(shape, generator=g) * 1e-4).bfloat16()
+    lr, wd = 3e-4, .1
+
+    def step():
+        gf = grad.float()
+        mom.lerp_(gf, .05)
+        u = gf.lerp(mom, .95)
+        x = u.float()
+        tall = x.shape[0] > x.shape[1]
+        if tall:
+            x = x.T
+        x = x / (x.norm() + 1e-7)
+        for _ in range(5):
+            a = x @ x.T
+            x = 3.4445 * x + (-4.775 * a + 2.0315 * (a @ a)) @ x
+        o = x.T if tall else x
+        o = o * max(1, shape[0] / shape[1]) ** .5
+        p.mul_(1 - lr * wd).add_(o, alpha=-lr)
+
+    step()
+    t0 = time.perf_counter()
+    step()
+    return time.perf_counter() - t0, threads
+
+
 def reference_cpu_step_time(layers=1, steps=3, warmup=1, seed=0):
     """Time the reference's CPU step on a bounded sample of config 2: ``layers``
     layers (94,384,128 params each) through torch.nn.utils.clip_grad_norm_
@@ -561,6 +596,20 @@ def run_config4(args):
                          "frac_executed": exec_flop / (step_ms / 1e3) / 1e12 / peak,
                          "note": "symmetric GEMMs skip lower tiles, so algorithmic FLOP/s can exceed the peak"},
             "per_matrix": per_shape, "clocks": clk.summary()}
+    if not args.no_cpu_baseline:
+        counts = {}
+        for q in opt.muon:
+            counts[tuple(q.shape)] = counts.get(tuple(q.shape), 0) + 1
+        est, threads, sample = 0.0, 1, {}
+        for shape, cnt in counts.items():
+            sec, threads = reference_muon_cpu_time(shape)
+            sample[f"{shape[0]}x{shape[1]}"] = sec
+            est += sec * cnt
+        line["cpu_baseline"] = {"value": est, "unit": "s/step", "cores": threads, "kind": "reference",
+                                "sample": "one Muon step (optimizer.py:52-61, FP32 orthogonalize) of each matrix "
+                                          "shape on the host cores, scaled by the shape counts; the AdamW group "
+                                          "(4% of the parameters, <1% of the work) is not included",
+                                "per_matrix_s": sample}
     print(json.dumps(line), flush=True)
 
 
