@@ -94,16 +94,23 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        """Start sampling every 50 ms and wait (up to 5 s) for the first sample,
+        so that even a short timed region is covered."""
+        import threading
+        self.first = []
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            reader = threading.Thread(target=lambda: self.first.append(self.proc.stdout.readline()), daemon=True)
+            reader.start()
+            reader.join(timeout=5.0)
         except Exception:
             self.proc = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        self.lines = [l for l in self.first if l and l.strip()]
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -111,7 +118,7 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
                 out = ""
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            self.lines += [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
