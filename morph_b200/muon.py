@@ -1,8 +1,9 @@
 """Hybrid Muon + AdamW on the B200 kernels.
 
-``gemm_bf16`` exposes kernel 4's tcgen05 GEMM. The Newton-Schulz
-orthogonalisation (streamtrain/optimizer.py:13-22) and the HybridMuonAdamW
-drop-in (streamtrain/optimizer.py:25-70) are built on it.
+``gemm16`` exposes kernel 4's tcgen05 GEMM (BF16 or FP16 operands, FP32
+accumulation). The Newton-Schulz orthogonalisation
+(streamtrain/optimizer.py:13-22), the batched Muon step and the
+HybridMuonAdamW drop-in (streamtrain/optimizer.py:25-70) are built on it.
 """
 from __future__ import annotations
 
