@@ -695,6 +695,7 @@ def reference_disk_update(path, size, gradient, step, lr, clip, chunk_elements=1
 
 def run_extra(args):
     """Measurements of the paths beside the configs' step (one GPU):
+    rows: kernel 3 (lazy row-sparse update) on a device-resident config-5 table;
     disk: DiskState.update on a 64M-parameter (3, size) state file, GPU arithmetic
           (morph_b200.disk_io) vs the reference's CPU loop, wall clock incl. file I/O;
     accum: microbatch gradient accumulation (512M FP32 window, BF16 grads), HBM roofline;
@@ -764,6 +765,36 @@ def run_extra(args):
                        "note": "wall clock incl. page-cache file reads/writes and fsync on the box's /tmp; "
                                "torch's CPU sqrt (vectorised) differs from IEEE sqrt by <= 1 ulp on some "
                                "elements, so w agrees within 1e-6 relative, not bit for bit"}
+    if args.extra in ("rows", "all"):
+        # kernel 3 on a device-resident table: DeviceDiskState.update_rows
+        from morph_b200.disk import DeviceDiskState
+        rows, cols = args.rows, 3072
+        k = rows // 10
+        gen = torch.Generator(device=device).manual_seed(3)
+        planes = torch.zeros(3, rows * cols, device=device)
+        planes[0].normal_(0, .02, generator=gen)
+        store = DeviceDiskState({"t": planes}, {"t": (rows, cols)})
+        idxs = [torch.randperm(rows, device=device, generator=gen)[:k].sort().values for _ in range(4)]
+        grads = (torch.randn(k, cols, device=device, generator=gen) * 1e-3).half()
+        for i in range(3):
+            store.update_rows("t", idxs[i % 4], grads, i + 1, 1e-4, 1.0, check=False)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        reps = 10
+        ev[0].record()
+        for i in range(reps):
+            store.update_rows("t", idxs[i % 4], grads, i + 4, 1e-4, 1.0, check=False)
+        ev[1].record()
+        torch.cuda.synchronize()
+        store.errors()
+        ms = ev[0].elapsed_time(ev[1]) / reps
+        algo = (26 * cols + 8) * k  # w, m, v read + written, f16 grad read, int64 index
+        out["rows"] = {"workload": f"update_rows on a device table [{rows},{cols}] (w, m, v planes), "
+                                   f"{k} sorted unique rows per launch, f16 grads (config-5 shapes, device-resident)",
+                       "ms": ms, "touched_params_per_s": k * cols / (ms / 1e3),
+                       "GB/s": algo / (ms / 1e3) / 1e9, "frac": algo / (ms / 1e3) / 1e9 / hbm,
+                       "algorithmic_bytes_per_launch": algo, "peak_hbm_gbs": hbm}
+        del planes, store, grads
+        torch.cuda.empty_cache()
     if args.extra in ("accum", "all"):
         from morph_b200.disk import accumulate_, norm_record
         n = 512 << 20
@@ -1162,7 +1193,8 @@ def main():
                     help="N > 1: NCCL all-gather rounds instead of kernel 1's peer stores")
     ap.add_argument("--c4-layers", type=int, default=32, help="profiling only: fewer layers than config 4")
     ap.add_argument("--ns-shape", default=None, help="profiling only, with --config 4: one matrix, e.g. 4096x4096")
-    ap.add_argument("--extra", choices=["disk", "accum", "export", "all"], default=None,
+    ap.add_argument("--rows", type=int, default=262144, help="--extra rows: table rows (profiling: fewer)")
+    ap.add_argument("--extra", choices=["disk", "rows", "accum", "export", "all"], default=None,
                     help="measure a path beside the configs' step instead (one GPU)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "morph":
