@@ -235,7 +235,8 @@ __host__ __device__ constexpr int bulk_smem_bytes() {
 struct SegCursor {
   int cur = -1;
   int64_t next_begin = -1;  // first tile of segment cur + 1 (INT64_MAX past the last)
-  __device__ __forceinline__ bool advance(const ApplyArgs& a, int64_t tile) {
+  template <class Args>
+  __device__ __forceinline__ bool advance(const Args& a, int64_t tile) {
     if (cur >= 0 && tile < next_begin) return false;
     int si = cur < 0 ? find_segment(a.segs, a.n_segs, tile) : cur;
     while (si + 1 < a.n_segs && __ldg(&a.segs[si + 1].tile_begin) <= tile) ++si;
@@ -416,20 +417,21 @@ struct StatsArgs {
   int32_t unscale;         // divide by state.scale
 };
 
-// Block-wide sum of (a, b) in a fixed order; result valid in thread 0.
+// Block-wide sum of (a, b) in a fixed order; result valid in thread 0. Any
+// block size that is a multiple of 32, up to 1024.
 __device__ __forceinline__ double2 block_sum2(double a, double b) {
-  __shared__ double2 red[kThreads / 32];
+  __shared__ double2 red[32];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     a += __shfl_down_sync(0xffffffffu, a, o);
     b += __shfl_down_sync(0xffffffffu, b, o);
   }
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
   if (lane == 0) red[warp] = make_double2(a, b);
   __syncthreads();
   double2 r = make_double2(0.0, 0.0);
   if (warp == 0) {
-    r = lane < kThreads / 32 ? red[lane] : make_double2(0.0, 0.0);
+    r = lane < warps ? red[lane] : make_double2(0.0, 0.0);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       r.x += __shfl_down_sync(0xffffffffu, r.x, o);
@@ -547,6 +549,44 @@ __device__ __forceinline__ void stats_elems(const uint4& q, bool unscale, const 
   }
 }
 
+// Per-CTA partial {sum of squares, nonfinite} of kernel 2, the last CTA's
+// fixed-order reduction into the step state, and the optional fused finalize.
+__device__ void stats_tail(const StatsArgs& a, double acc) {
+  mb_step_state* st = a.plan.state;
+  double2 r = block_sum2(acc, 0.0);
+  char* ws = static_cast<char*>(a.plan.workspace);
+  double2* partials = reinterpret_cast<double2*>(ws);
+  unsigned int* ticket = reinterpret_cast<unsigned int*>(ws + kTicketOffset);
+  __shared__ unsigned int s_last;
+  if (threadIdx.x == 0) {
+    r.y = isfinite(r.x) ? 0.0 : 1.0;
+    partials[blockIdx.x] = r;
+    __threadfence();
+    s_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // Last CTA: fixed-order reduction of the partials (deterministic for a grid).
+  double a0 = 0.0, b0 = 0.0;
+  for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
+    double2 qq = __ldcg(&partials[i]);
+    a0 += qq.x;
+    b0 += qq.y;
+  }
+  double2 tot = block_sum2(a0, b0);
+  if (threadIdx.x == 0) {
+    st->sumsq = tot.x;
+    st->nonfinite = tot.y;
+    *ticket = 0u;
+  }
+  __syncthreads();
+  if (a.fuse_finalize) {
+    __threadfence_block();
+    finalize_block(a.plan, a.fin);
+  }
+}
+
 #ifndef MB_STATS_U
 #define MB_STATS_U 4
 #endif
@@ -609,38 +649,149 @@ __global__ void __launch_bounds__(kThreads) k_grad_stats(StatsArgs a) {
       }
     }
   }
-  double2 r = block_sum2(acc, 0.0);
-  char* ws = static_cast<char*>(a.plan.workspace);
-  double2* partials = reinterpret_cast<double2*>(ws);
-  unsigned int* ticket = reinterpret_cast<unsigned int*>(ws + kTicketOffset);
-  __shared__ unsigned int s_last;
+  stats_tail(a, acc);
+}
+
+// Kernel 2, bulk-staged form (the default). One persistent CTA per SM (two
+// when shared memory allows) walks a contiguous run of tiles. Lane 0 of warp 0
+// streams chunks -- up to kSBTiles tiles of one segment -- of gradient bytes
+// into a ring of shared-memory stages with cp.async.bulk; the consumer warps
+// read 16-byte words from the stage and accumulate the FP64 sum of squares
+// (the same per-element arithmetic as k_grad_stats). Chunks that are not
+// 16-byte aligned or sized are read directly from global memory. Every wait is
+// bounded; a CTA that gives up counts its partial as nonfinite, so the step is
+// refused rather than clipped with a wrong norm.
+constexpr int kSBStages = 4;
+constexpr int kSBTiles = 4;
+constexpr int kSBWarps = 8;
+constexpr int kSBThreads = 32 * (kSBWarps + 1);
+
+template <int GDT>
+__host__ __device__ constexpr int sb_stage_bytes() {
+  return kSBTiles * kTile * (GDT == MB_F32 ? 4 : 2);
+}
+template <int GDT>
+__host__ __device__ constexpr int sb_smem_bytes() {
+  return kSBStages * sb_stage_bytes<GDT>() + 2 * kSBStages * 8 + 16;
+}
+
+struct StatsChunk {
+  const uint8_t* g;  // first byte of the chunk
+  int64_t n;         // elements
+  int tiles;         // tiles covered
+  bool bulk;
+};
+
+// The chunk starting at tile t of this CTA's run [.., t1) (same on both roles).
+template <int GDT>
+__device__ __forceinline__ StatsChunk stats_chunk(const StatsArgs& a, SegCursor& cur, mb_segment& seg,
+                                                  int64_t t, int64_t t1) {
+  constexpr int GB = GDT == MB_F32 ? 4 : 2;
+  if (cur.advance(a, t)) seg = a.segs[cur.cur];
+  int64_t tiles = cur.next_begin - t;
+  if (t1 - t < tiles) tiles = t1 - t;
+  if (tiles > kSBTiles) tiles = kSBTiles;
+  const int64_t e0 = (t - seg.tile_begin) * kTile;
+  int64_t n = seg.numel - e0;
+  if (n > tiles * kTile) n = tiles * kTile;
+  StatsChunk c;
+  c.g = static_cast<const uint8_t*>(seg.g) + e0 * GB;
+  c.n = n;
+  c.tiles = (int)tiles;
+  c.bulk = aligned(c.g, 16) && (n * GB) % 16 == 0 && n > 0;
+  return c;
+}
+
+template <int GDT, bool UNSCALE>
+__global__ void __launch_bounds__(kSBThreads) k_grad_stats_bulk(StatsArgs a) {
+  constexpr int GB = GDT == MB_F32 ? 4 : 2;
+  constexpr int STAGE = sb_stage_bytes<GDT>();
+  using T = typename Elem<GDT>::T;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSBStages * STAGE);
+  uint64_t* empty = full + kSBStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kSBStages);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    r.y = isfinite(r.x) ? 0.0 : 1.0;
-    partials[blockIdx.x] = r;
-    __threadfence();
-    s_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+    for (int i = 0; i < kSBStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kSBWarps);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
   }
   __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // Last CTA: fixed-order reduction of the partials (deterministic for a grid).
-  double a0 = 0.0, b0 = 0.0;
-  for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
-    double2 qq = __ldcg(&partials[i]);
-    a0 += qq.x;
-    b0 += qq.y;
-  }
-  double2 tot = block_sum2(a0, b0);
-  if (threadIdx.x == 0) {
-    st->sumsq = tot.x;
-    st->nonfinite = tot.y;
-    *ticket = 0u;
+  const int64_t per = (a.n_tiles + gridDim.x - 1) / gridDim.x;
+  const int64_t t0 = (int64_t)blockIdx.x * per;
+  const int64_t t1 = t0 + per < a.n_tiles ? t0 + per : a.n_tiles;
+  double acc = 0.0;
+  if (warp == 0) {
+    if (lane == 0) {
+      SegCursor cur;
+      mb_segment seg;
+      int k = 0;
+      int last_bulk[kSBStages];
+#pragma unroll
+      for (int i = 0; i < kSBStages; ++i) last_bulk[i] = -1;
+      for (int64_t t = t0; t < t1; ++k) {
+        const StatsChunk c = stats_chunk<GDT>(a, cur, seg, t, t1);
+        t += c.tiles;
+        const int s = k % kSBStages;
+        if (!mbar_wait(&empty[s], ((k / kSBStages) & 1) ^ 1, abort_flag)) break;
+        if (c.bulk) {
+          mbar_expect_tx(&full[s], (uint32_t)(c.n * GB));
+          bulk_load(smem + s * STAGE, c.g, (uint32_t)(c.n * GB), &full[s]);
+          last_bulk[s] = k;
+        } else {
+          mbar_arrive(&full[s]);
+        }
+      }
+      if (*abort_flag) {
+#pragma unroll
+        for (int i = 0; i < kSBStages; ++i) {
+          if (last_bulk[i] < 0) continue;
+          const uint32_t parity = (last_bulk[i] / kSBStages) & 1;
+          const uint64_t w0 = globaltimer();
+          while (!mbar_try_wait(&full[i], parity) && globaltimer() - w0 < kWaitLimitNs) {
+          }
+        }
+      }
+    }
+  } else {
+    const int ct = threadIdx.x - 32;
+    constexpr int nthr = 32 * kSBWarps;
+    mb_step_state* st = a.plan.state;
+    const GradPrep prep = make_prep(UNSCALE ? __double2float_rn(st->scale) : 1.0f, 1.0f);
+    SegCursor cur;
+    mb_segment seg;
+    int k = 0;
+    for (int64_t t = t0; t < t1; ++k) {
+      const StatsChunk c = stats_chunk<GDT>(a, cur, seg, t, t1);
+      t += c.tiles;
+      const int s = k % kSBStages;
+      if (!mbar_wait(&full[s], (k / kSBStages) & 1, abort_flag)) break;
+      if (c.bulk) {
+        const uint4* words = reinterpret_cast<const uint4*>(smem + s * STAGE);
+        const int nw = (int)(c.n * GB / 16);
+        for (int w = ct; w < nw; w += nthr) stats_elems<GDT>(words[w], UNSCALE, prep, acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      } else {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        const T* gp = reinterpret_cast<const T*>(c.g);
+        for (int64_t e = ct; e < c.n; e += nthr) {
+          float y = to_f32(gp[e]);
+          if (UNSCALE) y = prep(y);
+          const double d = (double)y;
+          acc = __fma_rn(d, d, acc);
+        }
+      }
+    }
   }
   __syncthreads();
-  if (a.fuse_finalize) {
-    __threadfence_block();
-    finalize_block(a.plan, a.fin);
-  }
+  if (*abort_flag) acc = nan("");  // refuse the step: the partial counts as nonfinite
+  stats_tail(a, acc);
 }
 
 __global__ void __launch_bounds__(kThreads) k_step_finalize(mb_adamw_plan p, mb_finalize_opts f) {
@@ -702,13 +853,13 @@ bool use_bulk_apply() {
 }
 
 // Opt a bulk kernel into its dynamic shared memory (once per kernel and device).
-bool bulk_ready(ApplyFn fn, int smem) {
+bool bulk_ready(const void* fn, int smem) {
   static std::mutex mu;
   static std::map<std::pair<const void*, int>, bool> done;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
-  auto key = std::make_pair(reinterpret_cast<const void*>(fn), dev);
+  auto key = std::make_pair(fn, dev);
   auto it = done.find(key);
   if (it != done.end()) return it->second;
   bool ok = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess;
@@ -747,6 +898,32 @@ UpdateFn pick_update(int gdt, int odt) {
   }
 }
 using StatsFn = void (*)(StatsArgs);
+
+struct StatsBulk {
+  StatsFn fn;
+  int smem;
+};
+StatsBulk pick_stats_bulk(int gdt, bool unscale) {
+  switch (gdt) {
+    case MB_F32:
+      return {unscale ? &k_grad_stats_bulk<MB_F32, true> : &k_grad_stats_bulk<MB_F32, false>, sb_smem_bytes<MB_F32>()};
+    case MB_F16:
+      return {unscale ? &k_grad_stats_bulk<MB_F16, true> : &k_grad_stats_bulk<MB_F16, false>, sb_smem_bytes<MB_F16>()};
+    case MB_BF16:
+      return {unscale ? &k_grad_stats_bulk<MB_BF16, true> : &k_grad_stats_bulk<MB_BF16, false>,
+              sb_smem_bytes<MB_BF16>()};
+    default: return {nullptr, 0};
+  }
+}
+
+// Kernel 2's form: bulk-staged unless MB_STATS_KERNEL=direct (read once).
+bool use_bulk_stats() {
+  static const bool bulk = [] {
+    const char* e = getenv("MB_STATS_KERNEL");
+    return !(e && strcmp(e, "direct") == 0);
+  }();
+  return bulk;
+}
 StatsFn pick_stats(int gdt, bool unscale) {
   switch (gdt) {
     case MB_F32: return unscale ? &k_grad_stats<MB_F32, true> : &k_grad_stats<MB_F32, false>;
@@ -840,6 +1017,19 @@ MB_API int mb_grad_stats(const mb_adamw_plan* p, const mb_finalize_opts* fin, mb
   a.fin = fin ? *fin : mb_finalize_opts{};
   a.fuse_finalize = fin != nullptr;
   a.unscale = unscale;
+  StatsBulk bulk = pick_stats_bulk(p->grad_dtype, unscale);
+  if (use_bulk_stats() && bulk.fn && bulk_ready(reinterpret_cast<const void*>(bulk.fn), bulk.smem)) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bulk.fn, kSBThreads, bulk.smem) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    int64_t grid = (int64_t)sm_count() * per_sm;
+    if (grid > p->n_tiles) grid = p->n_tiles;
+    if (grid > kMaxStatsBlocks) grid = kMaxStatsBlocks;
+    if (grid < 1) grid = 1;
+    bulk.fn<<<(int)grid, kSBThreads, bulk.smem, (cudaStream_t)stream>>>(a);
+    return launch_status();
+  }
   int grid = grid_for(reinterpret_cast<const void*>(fn), p->n_tiles);
   if (grid > kMaxStatsBlocks) grid = kMaxStatsBlocks;
   fn<<<grid, kThreads, 0, (cudaStream_t)stream>>>(a);
@@ -871,7 +1061,7 @@ MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* p, int64_t tile_lo, int64_t
   a.tile_lo = tile_lo;
   a.n_tiles = tile_hi;
   a.n_segs = p->n_segs;
-  if (use_bulk_apply() && bulk.fn && bulk_ready(bulk.fn, bulk.smem)) {
+  if (use_bulk_apply() && bulk.fn && bulk_ready(reinterpret_cast<const void*>(bulk.fn), bulk.smem)) {
     // kBulkCtasPerSm CTAs per SM; max_ctas counts register-staged CTAs (3 per SM)
     int64_t grid = (int64_t)sm_count() * kBulkCtasPerSm;
     if (max_ctas > 0) grid = max_ctas * kBulkCtasPerSm / 3 > 0 ? max_ctas * kBulkCtasPerSm / 3 : 1;
@@ -896,7 +1086,7 @@ MB_API int mb_adamw_apply_tiles_peers(const mb_adamw_plan* p, int64_t tile_lo, i
     if (peer_deltas[i] % 16) return MB_ERR_ALIGN;  // keeps the copies' vector alignment
   if (tile_lo == tile_hi) return MB_OK;
   BulkFn bulk = pick_apply_bulk(p->grad_dtype, p->out_dtype);
-  if (!bulk.fn || !bulk_ready(bulk.fn, bulk.smem)) return MB_ERR_CUDA;
+  if (!bulk.fn || !bulk_ready(reinterpret_cast<const void*>(bulk.fn), bulk.smem)) return MB_ERR_CUDA;
   ApplyArgs a{};
   a.segs = p->segs;
   a.groups = p->groups;
