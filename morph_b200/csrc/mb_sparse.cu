@@ -8,12 +8,15 @@
 //
 // Layout: w, m, v are [rows, cols] FP32 planes; grads is [k, cols] with
 // gradient row r belonging to table row idx[r]. One CTA updates one touched
-// row per iteration, sweeping it in coalesced passes of 1024 elements; the
-// grid is persistent and strides over the k touched rows.
+// row per iteration, sweeping it in coalesced passes of 1024 elements, up to
+// three passes' loads issued together; the grid is persistent and strides
+// over the k touched rows.
 #include "mb_common.cuh"
 
 namespace mb {
 namespace {
+
+constexpr int kRowPasses = 3;  // 1024-element sweeps of a row loaded together
 
 template <int GDT>
 __global__ void __launch_bounds__(kThreads) k_sparse_rows(float* __restrict__ w, float* __restrict__ m,
@@ -38,26 +41,45 @@ __global__ void __launch_bounds__(kThreads) k_sparse_rows(float* __restrict__ w,
     float* mr = m + row * cols;
     float* vr = v + row * cols;
     int64_t gbase = r * cols;
-    for (int64_t e = (int64_t)threadIdx.x * kQuad; e < cols; e += kHalf) {
-      if (vec) {
-        float g[4];
-        load4<GDT>(grads, gbase + e, g);
-        float4 a = ld4f(wr + e), b = ld4f(mr + e), c = ld4f(vr + e);
-        float ww[4] = {a.x, a.y, a.z, a.w}, mm[4] = {b.x, b.y, b.z, b.w}, vv[4] = {c.x, c.y, c.z, c.w};
+    if (vec) {
+      // up to kRowPasses sweeps of 1024 elements: every load of the batch is issued
+      // before any arithmetic (a 3072-wide row is one batch)
+      for (int64_t e0 = (int64_t)threadIdx.x * kQuad; e0 < cols; e0 += kRowPasses * kHalf) {
+        float4 a[kRowPasses], b[kRowPasses], c[kRowPasses];
+        float g[kRowPasses][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) adam_elem(ww[j], mm[j], vv[j], prep(g[j]), s);
-        st4f(wr + e, make_float4(ww[0], ww[1], ww[2], ww[3]));
-        st4f(mr + e, make_float4(mm[0], mm[1], mm[2], mm[3]));
-        st4f(vr + e, make_float4(vv[0], vv[1], vv[2], vv[3]));
-      } else {
-        int64_t end = e + kQuad < cols ? e + kQuad : cols;
-        for (int64_t j = e; j < end; ++j) {
-          float ww = wr[j], mm = mr[j], vv = vr[j];
-          adam_elem(ww, mm, vv, prep(load1<GDT>(grads, gbase + j)), s);
-          wr[j] = ww;
-          mr[j] = mm;
-          vr[j] = vv;
+        for (int u = 0; u < kRowPasses; ++u) {
+          const int64_t e = e0 + u * kHalf;
+          if (e < cols) {  // cols % 4 == 0: a quad is all in or all out
+            load4<GDT>(grads, gbase + e, g[u]);
+            a[u] = ld4f(wr + e);
+            b[u] = ld4f(mr + e);
+            c[u] = ld4f(vr + e);
+          }
         }
+#pragma unroll
+        for (int u = 0; u < kRowPasses; ++u) {
+          const int64_t e = e0 + u * kHalf;
+          if (e >= cols) continue;
+          float ww[4] = {a[u].x, a[u].y, a[u].z, a[u].w}, mm[4] = {b[u].x, b[u].y, b[u].z, b[u].w};
+          float vv[4] = {c[u].x, c[u].y, c[u].z, c[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) adam_elem(ww[j], mm[j], vv[j], prep(g[u][j]), s);
+          st4f(wr + e, make_float4(ww[0], ww[1], ww[2], ww[3]));
+          st4f(mr + e, make_float4(mm[0], mm[1], mm[2], mm[3]));
+          st4f(vr + e, make_float4(vv[0], vv[1], vv[2], vv[3]));
+        }
+      }
+      continue;
+    }
+    for (int64_t e = (int64_t)threadIdx.x * kQuad; e < cols; e += kHalf) {
+      const int64_t end = e + kQuad < cols ? e + kQuad : cols;
+      for (int64_t j = e; j < end; ++j) {
+        float ww = wr[j], mm = mr[j], vv = vr[j];
+        adam_elem(ww, mm, vv, prep(load1<GDT>(grads, gbase + j)), s);
+        wr[j] = ww;
+        mr[j] = mm;
+        vr[j] = vv;
       }
     }
   }
