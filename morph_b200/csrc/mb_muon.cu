@@ -18,8 +18,8 @@
 //                    norm divisor);
 //   k_ns_normalize   x = u / (||u|| + 1e-7) as X [mp, np] and its transpose
 //                    XT [np, mp] (mp, np = m, n rounded up to 256, zero
-//                    padding written explicitly) through 32x32 tiles, both
-//                    orientations read coalesced;
+//                    padding written explicitly) through 32x64 tiles with
+//                    vector loads and stores, both orientations coalesced;
 //   15 GEMMs         per iteration: A = X X^T; M = a I + b A + c A A (one
 //                    FP32 epilogue, rounded once); X' = M X (reads XT, writes
 //                    X' and X'^T). The last X' = M X applies the update
@@ -172,40 +172,81 @@ __global__ void __launch_bounds__(kThreads) k_muon_sumsq(MuonSrc t, MuonParams p
   }
 }
 
-// grid (cols_p / 32, rows_p / 32, batch), block (32, 8): one 32x32 tile of u
-// (the matrix in its stored orientation, padded to rows_p x cols_p) per CTA,
-// read row by row (coalesced). The tile goes to D [rows_p, cols_p] as is and
-// to T [cols_p, rows_p] transposed through shared memory. Wide matrices: D is
-// X and T is XT; tall: D is XT and T is X. Values are prescale * u / divisor,
-// zero in the padding. `prescale` is a power of two (exact); it lifts the first
-// iterate's elements (RMS 1/sqrt(m n)) toward their converged size (1/sqrt(n))
-// so FP16 operands stay out of the subnormal range, and the first iteration's
-// GEMMs divide it back out exactly.
+// Read-only Nesterov blend of four consecutive elements (the momentum already
+// holds this step's value): u = fma(w - 1, m - g, m), or the FP32 source itself.
+template <int GDT>
+__device__ __forceinline__ void muon_u4_read(const float* mom, const void* src, const MuonParams& p, int64_t e,
+                                             float (&u)[4]) {
+  if (mom == nullptr) {
+    load4<MB_F32>(src, e, u);
+    return;
+  }
+  float g[4];
+  load4<GDT>(src, e, g);
+  const float4 m4 = *reinterpret_cast<const float4*>(mom + e);
+  const float mo[4] = {m4.x, m4.y, m4.z, m4.w};
+#pragma unroll
+  for (int h = 0; h < 4; ++h) u[h] = __fmaf_rn(__fsub_rn(p.nesterov, 1.0f), __fsub_rn(mo[h], g[h]), mo[h]);
+}
+
+// grid (cols_p / 64, rows_p / 32, batch), 256 threads: one 32 x 64 tile of u
+// (the matrix in its stored orientation, padded to rows_p x cols_p) per CTA.
+// Thread (ty, tx) of a 16 x 16 grid reads rows ty and ty + 16, columns 4tx..4tx+3
+// (16-byte momentum / 8-byte gradient loads when `vec`), writes them to D
+// [rows_p, cols_p] as 8-byte vectors, and after a shared-memory transpose
+// writes 8 consecutive elements of one row of T [cols_p, rows_p]. Wide
+// matrices: D is X and T is XT; tall: D is XT and T is X. Values are
+// prescale * u / divisor, zero in the padding. `prescale` is a power of two
+// (exact); it lifts the first iterate's elements (RMS 1/sqrt(m n)) toward their
+// converged size (1/sqrt(n)) so FP16 operands stay out of the subnormal range,
+// and the first iteration's GEMMs divide it back out exactly.
 template <int GDT, int OUT>
 __global__ void __launch_bounds__(256) k_ns_normalize(MuonSrc t, MuonParams p, int64_t rows, int64_t cols,
                                                       int64_t ld_d, int64_t ld_t, size_t stride, const float* divisors,
-                                                      float prescale, void* Dv, void* Tv) {
+                                                      float prescale, void* Dv, void* Tv, bool vec) {
   using T = typename Elem<OUT>::T;
   const int b = blockIdx.z;
   T* D = static_cast<T*>(Dv) + stride * b;
   T* Tt = static_cast<T*>(Tv) + stride * b;
-  float* mom = t.mom[b];
+  const float* mom = t.mom[b];
   const void* src = t.src[b];
-  __shared__ float tile[32][33];
+  __shared__ float tile[32][65];
   const float d = divisors[b];
-  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
-  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 64;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int64_t r = r0 + ty + 8 * k, c = c0 + tx;
-    float val = 0.0f;
-    if (r < rows && c < cols) val = __fmul_rn(__fdiv_rn(muon_u<GDT>(mom, src, p, r * cols + c, false), d), prescale);
-    D[r * ld_d + c] = from_f32<OUT>(val);
-    tile[ty + 8 * k][tx] = val;
+  for (int h = 0; h < 2; ++h) {
+    const int lr = ty + 16 * h, lc = 4 * tx;
+    const int64_t r = r0 + lr, c = c0 + lc;
+    float val[4];
+    if (vec && r < rows && c + 4 <= cols) {
+      float u[4];
+      muon_u4_read<GDT>(mom, src, p, r * cols + c, u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) val[j] = __fmul_rn(__fdiv_rn(u[j], d), prescale);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        val[j] = 0.0f;
+        if (r < rows && c + j < cols)
+          val[j] = __fmul_rn(__fdiv_rn(muon_u<GDT>(const_cast<float*>(mom), src, p, r * cols + c + j, false), d),
+                             prescale);
+      }
+    }
+    store4<OUT>(D, r * ld_d + c, val);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tile[lr][lc + j] = val[j];
   }
   __syncthreads();
+  const int tc = tid >> 2, tr0 = (tid & 3) * 8;
+  float lo[4], hi[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) Tt[(c0 + ty + 8 * k) * ld_t + r0 + tx] = from_f32<OUT>(tile[tx][ty + 8 * k]);
+  for (int i = 0; i < 4; ++i) {
+    lo[i] = tile[tr0 + i][tc];
+    hi[i] = tile[tr0 + 4 + i][tc];
+  }
+  store4<OUT>(Tt, (c0 + tc) * ld_t + r0 + tr0, lo);
+  store4<OUT>(Tt, (c0 + tc) * ld_t + r0 + tr0 + 4, hi);
 }
 
 // FP32 result in the input's orientation (orthogonalize's return value).
@@ -249,23 +290,23 @@ int launch_sumsq(const MuonSrc& t, const MuonParams& p, int batch, int64_t total
 
 template <int GDT, int OUT>
 int launch_normalize(const MuonSrc& t, const MuonParams& p, int batch, int64_t rows, int64_t cols, const Layout& L,
-                     char* ws, float ps, cudaStream_t s) {
+                     char* ws, float ps, bool vec, cudaStream_t s) {
   const bool tall = rows > cols;
   // the stored orientation of u, padded: wide [mp, np], tall [np, mp]
   const int64_t rp = tall ? L.np : L.mp, cp = tall ? L.mp : L.np;
   void* D = ws + (tall ? L.t0 : L.x);
   void* T = ws + (tall ? L.x : L.t0);
-  dim3 blk(32, 8), grd((unsigned)(cp / 32), (unsigned)(rp / 32), (unsigned)batch);
-  k_ns_normalize<GDT, OUT><<<grd, blk, 0, s>>>(t, p, rows, cols, cp, rp, (size_t)L.mp * L.np,
-                                               reinterpret_cast<const float*>(ws + L.divisors), ps, D, T);
+  dim3 grd((unsigned)(cp / 64), (unsigned)(rp / 32), (unsigned)batch);
+  k_ns_normalize<GDT, OUT><<<grd, 256, 0, s>>>(t, p, rows, cols, cp, rp, (size_t)L.mp * L.np,
+                                               reinterpret_cast<const float*>(ws + L.divisors), ps, D, T, vec);
   return cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA;
 }
 
 template <int GDT>
 int launch_normalize_any(int out, const MuonSrc& t, const MuonParams& p, int batch, int64_t rows, int64_t cols,
-                         const Layout& L, char* ws, float ps, cudaStream_t s) {
-  if (out == MB_F16) return launch_normalize<GDT, MB_F16>(t, p, batch, rows, cols, L, ws, ps, s);
-  return launch_normalize<GDT, MB_BF16>(t, p, batch, rows, cols, L, ws, ps, s);
+                         const Layout& L, char* ws, float ps, bool vec, cudaStream_t s) {
+  if (out == MB_F16) return launch_normalize<GDT, MB_F16>(t, p, batch, rows, cols, L, ws, ps, vec, s);
+  return launch_normalize<GDT, MB_BF16>(t, p, batch, rows, cols, L, ws, ps, vec, s);
 }
 
 // The final update of a batch (null for orthogonalize, which keeps O).
@@ -290,6 +331,7 @@ int ns_core(const MuonSrc& t, const MuonParams& p, int gdt, int batch, int64_t r
     const uintptr_t ga = t.mom[b] == nullptr || gdt == MB_F32 ? 16 : 8;
     vec = aligned(t.src[b], ga) && (t.mom[b] == nullptr || aligned(t.mom[b], 16));
   }
+  const bool vec_rows = vec && cols % 4 == 0;  // every row starts on a 16-byte boundary
   if (cudaMemsetAsync(ws + L.tickets, 0, sizeof(unsigned) * batch, s) != cudaSuccess) return MB_ERR_CUDA;
   int rc;
   switch (gdt) {
@@ -302,9 +344,9 @@ int ns_core(const MuonSrc& t, const MuonParams& p, int gdt, int batch, int64_t r
   const int64_t m = rows < cols ? rows : cols;
   const float ps = prescale_for(m);
   switch (gdt) {
-    case MB_F32: rc = launch_normalize_any<MB_F32>(dtype, t, p, batch, rows, cols, L, ws, ps, s); break;
-    case MB_F16: rc = launch_normalize_any<MB_F16>(dtype, t, p, batch, rows, cols, L, ws, ps, s); break;
-    default: rc = launch_normalize_any<MB_BF16>(dtype, t, p, batch, rows, cols, L, ws, ps, s); break;
+    case MB_F32: rc = launch_normalize_any<MB_F32>(dtype, t, p, batch, rows, cols, L, ws, ps, vec_rows, s); break;
+    case MB_F16: rc = launch_normalize_any<MB_F16>(dtype, t, p, batch, rows, cols, L, ws, ps, vec_rows, s); break;
+    default: rc = launch_normalize_any<MB_BF16>(dtype, t, p, batch, rows, cols, L, ws, ps, vec_rows, s); break;
   }
   if (rc) return rc;
   const int64_t mp = L.mp, np = L.np, sx = mp * np, sa = mp * mp;
