@@ -93,6 +93,28 @@ class GpuDiskUpdater:
         entry = self.store.entries[name]
         size = int(entry["size"])
         path = os.path.join(str(self.store.root), entry["file"])
+        mapped = np.memmap(path, dtype=np.float32, mode="r+", shape=(3, size))
+        self._run(name, mapped, [mapped], gradient, step, lr, clip, chunk_elements)
+        _flush_and_fsync(mapped, path)
+
+    def update_cached(self, name, values, gradient, step, lr, clip, chunk_elements=1048576):
+        """The cache-hit path of CachedDiskState.update (state_cache.py:111-137):
+        the entry's planes come from ``values`` (its RAM copy, (3, size) FP32)
+        and every chunk is written to both ``values`` and the file before the
+        fault hook, then the file is flushed and fsynced."""
+        entry = self.store.entries[name]
+        size = int(entry["size"])
+        if values.shape != (3, size) or values.dtype != np.float32:
+            raise ValueError(f"{name}: cached planes must be float32 of shape (3, {size})")
+        path = os.path.join(str(self.store.root), entry["file"])
+        mapped = np.memmap(path, dtype=np.float32, mode="r+", shape=(3, size))
+        self._run(name, values, [values, mapped], gradient, step, lr, clip, chunk_elements)
+        _flush_and_fsync(mapped, path)
+
+    def _run(self, name, source, sinks, gradient, step, lr, clip, chunk_elements):
+        """Stream the (3, size) planes of ``source`` through the device windows
+        and write the updated planes to every array of ``sinks`` chunk by chunk."""
+        size = int(source.shape[1])
         g = gradient.reshape(-1)
         if g.numel() != size:
             raise ValueError(f"{name}: gradient must have {size} elements")
@@ -100,13 +122,14 @@ class GpuDiskUpdater:
             raise ValueError(f"{name}: gradient is on {g.device}, the updater on {self.device}")
         g = g.contiguous()
         s = disk_host_scalars(float(lr), int(step), float(clip))
-        mapped = np.memmap(path, dtype=np.float32, mode="r+", shape=(3, size))
         # windows hold whole reference chunks, so writes and fault calls fall where the reference's do
         W = max(chunk_elements, self.window // chunk_elements * chunk_elements)
         if W > self.capacity:
             torch.cuda.synchronize(self.device)
             self._alloc(W)
         n_win = -(-size // W)
+        if n_win == 0:
+            return
         lib = _lib.lib()
         compute = torch.cuda.current_stream(self.device)
         start = torch.cuda.Event()
@@ -114,12 +137,12 @@ class GpuDiskUpdater:
         self.h2d.wait_event(start)
 
         def stage(j):
-            """Read window j from the file and enqueue its copies and update."""
+            """Read window j from the source and enqueue its copies and update."""
             b, lo = j % 2, j * W
             n = min(W, size - lo)
             host = self.host[b][:3 * n].view(3, n)
             dev = self.dev[b][:3 * n].view(3, n)
-            _parallel_copy(host.numpy(), mapped[:, lo:lo + n])  # buffer b was written back already
+            _parallel_copy(host.numpy(), source[:, lo:lo + n])  # buffer b was written back already
             with torch.cuda.stream(self.h2d):
                 if j >= 2:
                     self.h2d.wait_event(self.done[b])  # device window b's copy-back is complete
@@ -150,7 +173,8 @@ class GpuDiskUpdater:
             host = self.host[b][:3 * n].view(3, n).numpy()
             for c0 in range(0, n, chunk_elements):  # the reference's write and fault granularity
                 c1 = min(c0 + chunk_elements, n)
-                _parallel_copy(mapped[:, lo + c0:lo + c1], host[:, c0:c1])
+                for sink in sinks:
+                    _parallel_copy(sink[:, lo + c0:lo + c1], host[:, c0:c1])
                 self._fault('partial_state_write')
 
         stage(0)
@@ -159,13 +183,16 @@ class GpuDiskUpdater:
                 stage(j + 1)  # window (j + 1) % 2 was written back in iteration j - 1
             write_back(j)
         compute.wait_event(self.done[(n_win - 1) % 2])
-        mapped.flush()
-        del mapped
-        fd = os.open(path, os.O_RDWR)
-        try:
-            os.fsync(fd)
-        finally:
-            os.close(fd)
+
+
+def _flush_and_fsync(mapped, path):
+    mapped.flush()
+    del mapped
+    fd = os.open(path, os.O_RDWR)
+    try:
+        os.fsync(fd)
+    finally:
+        os.close(fd)
 
 
 def install(store, device="cuda", window_elements: int = 1 << 24) -> GpuDiskUpdater:
@@ -188,6 +215,39 @@ def patch_class(cls, device="cuda", window_elements: int = 1 << 24):
         if updater is None:
             updater = self.__dict__["_mb_gpu_updater"] = GpuDiskUpdater(self, device, window_elements)
         return updater.update(name, gradient, step, lr, clip, chunk_elements)
+
+    cls.update = update
+
+    def restore():
+        cls.update = original
+    return restore
+
+
+def patch_cached_class(cls, device="cuda", window_elements: int = 1 << 24):
+    """The same for a CachedDiskState-like class (state_cache.py:103-140: a
+    bounded RAM cache ``_cache`` of (3, size) planes under ``_cache_lock``,
+    counters in ``_cache_stats``, ``_drop`` on failure): a cache hit updates the
+    RAM copy and the file from the GPU (``update_cached``), a miss runs the
+    file path. Returns a function that restores the original method."""
+    original = cls.update
+
+    def update(self, name, gradient, step, lr, clip, chunk_elements=1048576):
+        updater = self.__dict__.get("_mb_gpu_updater")
+        if updater is None:
+            updater = self.__dict__["_mb_gpu_updater"] = GpuDiskUpdater(self, device, window_elements)
+        with self._cache_lock:
+            values = self._cache.get(name)
+            if values is None:
+                self._cache_stats["misses"] += 1
+                return updater.update(name, gradient, step, lr, clip, chunk_elements)
+            self._cache.move_to_end(name)
+            self._cache_stats["hits"] += 1
+            self._cache_stats["estimated_bytes_avoided"] += values.nbytes
+            try:
+                updater.update_cached(name, values, gradient, step, lr, clip, chunk_elements)
+            except BaseException:
+                self._drop(name)
+                raise
 
     cls.update = update
 

@@ -119,3 +119,68 @@ def test_patch_class_routes_every_instance(cuda, tmp_path):
         restore()
     with pytest.raises(AssertionError):
         s1.update("a", g, 2, 1e-3, .5)
+
+
+class CachedFileStore(FileStore):
+    """The parts of the reference's CachedDiskState the cached patch uses:
+    a RAM cache of (3, size) planes, its lock, counters and _drop."""
+
+    def __init__(self, root, arrays, cached, fail_at=None):
+        import collections
+        import threading
+        super().__init__(root, arrays, fail_at)
+        self._cache_lock = threading.RLock()
+        self._cache = collections.OrderedDict((n, self.planes(n).copy()) for n in cached)
+        self._cache_stats = {"hits": 0, "misses": 0, "estimated_bytes_avoided": 0}
+        self.dropped = []
+
+    def update(self, *args, **kwargs):
+        raise AssertionError("the original update must not run while patched")
+
+    def _drop(self, name):
+        self._cache.pop(name, None)
+        self.dropped.append(name)
+
+
+def test_patch_cached_class_hit_and_miss(cuda, tmp_path):
+    """state_cache.py:103-140 semantics: a hit updates the RAM copy and the
+    file (byte-identical to each other and to the oracle), a miss updates the
+    file only; the counters move as the reference's do."""
+    from morph_b200.disk_io import patch_cached_class
+    arrays = {"hot": _planes(5000, 51), "cold": _planes(7000, 52)}
+    store = CachedFileStore(tmp_path, arrays, cached=["hot"])
+    restore = patch_cached_class(CachedFileStore, cuda, window_elements=2048)
+    try:
+        ref = {k: v.copy() for k, v in arrays.items()}
+        for step in (1, 2):
+            for name, p in arrays.items():
+                g = torch.from_numpy(orc.rng(step * 7 + len(name)).standard_normal(p.shape[1]).astype(np.float32))
+                store.update(name, g, step, 1e-3, .5, chunk_elements=1000)
+                ref[name] = _oracle(ref[name], g.numpy(), step, 1e-3, .5)
+        torch.cuda.synchronize()
+        for name in arrays:
+            np.testing.assert_array_equal(store.planes(name), ref[name])
+        np.testing.assert_array_equal(store._cache["hot"], ref["hot"])
+        assert store._cache_stats["hits"] == 2 and store._cache_stats["misses"] == 2
+    finally:
+        restore()
+
+
+def test_patch_cached_class_fault_drops_the_entry(cuda, tmp_path):
+    from morph_b200.disk_io import patch_cached_class
+    n, chunk = 5000, 1000
+    planes = _planes(n, 53)
+    store = CachedFileStore(tmp_path, {"hot": planes}, cached=["hot"], fail_at=3)
+    restore = patch_cached_class(CachedFileStore, cuda, window_elements=2000)
+    try:
+        g = torch.from_numpy(orc.rng(54).standard_normal(n).astype(np.float32))
+        with pytest.raises(RuntimeError, match="injected"):
+            store.update("hot", g, 1, 1e-3, 1.0, chunk_elements=chunk)
+        torch.cuda.synchronize()
+        assert store.dropped == ["hot"] and "hot" not in store._cache
+        ref = _oracle(planes, g.numpy(), 1, 1e-3, 1.0)
+        got = store.planes("hot")
+        np.testing.assert_array_equal(got[:, :3 * chunk], ref[:, :3 * chunk])
+        np.testing.assert_array_equal(got[:, 3 * chunk:], planes[:, 3 * chunk:])
+    finally:
+        restore()
