@@ -848,6 +848,84 @@ def run_extra(args):
     print(json.dumps(out), flush=True)
 
 
+def run_config1(args):
+    """Config 1 (and the latency side of config 3): 64 x [128, 128] FP32 masters,
+    FP16 grads x 2^16 with the device loss scale (2^16, growth 2000), lr 3e-4,
+    betas (.9, .95), eps 1e-8, wd .1, FP16 copy of the weights every step.
+    Launch-bound: times the eager AdamW.step and the same step replayed from a
+    CUDA graph, next to the reference's CPU step (unscale + torch AdamW)."""
+    from morph_b200 import AdamW, DynamicLossScale
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    gen = torch.Generator(device=device).manual_seed(1234)
+    ps = [torch.nn.Parameter(torch.randn(128, 128, device=device, generator=gen) * .02) for _ in range(64)]
+    for p in ps:
+        p.grad_dtype = None
+        p.grad = (torch.randn(128, 128, device=device, generator=gen) * 1e-3 * 65536.0).half()
+    scaler = DynamicLossScale(scale=65536.0, growth_interval=2000, device=device)
+    opt = AdamW(ps, lr=3e-4, betas=(.9, .95), eps=1e-8, weight_decay=.1, loss_scale=scaler,
+                low_precision=torch.float16)
+    reps = 200
+    for _ in range(max(3, args.warmup)):
+        opt.step()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    t0 = time.perf_counter()
+    ev[0].record()
+    for _ in range(reps):
+        opt.step()
+    ev[1].record()
+    torch.cuda.synchronize()
+    eager_us = (time.perf_counter() - t0) / reps * 1e6
+    eager_dev_us = ev[0].elapsed_time(ev[1]) / reps * 1e3
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+        opt.step()
+    torch.cuda.current_stream(device).wait_stream(side)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ev[0].record()
+    for _ in range(reps):
+        graph.replay()
+    ev[1].record()
+    torch.cuda.synchronize()
+    graph_us = (time.perf_counter() - t0) / reps * 1e6
+    # the reference's CPU step on the same shapes: unscale the FP16 grads, torch AdamW
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    cp = [torch.nn.Parameter(p.detach().cpu().clone()) for p in ps]
+    cg = [p.grad.cpu() for p in ps]
+    copt = torch.optim.AdamW(cp, lr=3e-4, betas=(.9, .95), eps=1e-8, weight_decay=.1, foreach=False)
+
+    def cpu_step():
+        for q, g in zip(cp, cg):
+            q.grad = g.float() / 65536.0
+        copt.step()
+        [q.detach().half() for q in cp]  # the FP16 weights of each step
+
+    for _ in range(3):
+        cpu_step()
+    t0 = time.perf_counter()
+    for _ in range(20):
+        cpu_step()
+    cpu_us = (time.perf_counter() - t0) / 20 * 1e6
+    n = 64 * 128 * 128
+    line = {"metric": "AdamW step latency, config 1 (64 x [128,128], FP16 grads, loss scale 2^16, FP16 copy)",
+            "value": graph_us, "unit": "us/step", "n_gpus": 1, "steps": reps, "warmup": max(3, args.warmup),
+            "higher_is_better": False, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config1: 1,048,576 params", "params": n},
+            "eager_us_per_step": eager_us, "eager_device_us_per_step": eager_dev_us,
+            "graph_replay_us_per_step": graph_us,
+            "cpu_baseline": {"value": cpu_us, "unit": "us/step", "cores": threads, "kind": "reference",
+                             "sample": "unscale + torch.optim.AdamW(foreach=False) + FP16 copy on the same shapes"},
+            "gpu_launches_per_step": 2}
+    print(json.dumps(line), flush=True)
+
+
 def run_config5(args, rank=0, world=1, local_rank=0):
     """Config 5: lazy row-sparse AdamW with the [262144, 3072] table's w, m, v in
     pinned host memory, 10% of rows (sorted unique int64) touched per step with
@@ -1184,9 +1262,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=42, help="profiling only: fewer layers than config 2")
     ap.add_argument("--no-embedding", action="store_true", help="profiling only: drop the embedding")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 4, 5],
-                    help="2 (default): the dense AdamW step; 4: the hybrid Muon+AdamW step; "
-                         "5: row-sparse AdamW on pinned-host state")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 4, 5],
+                    help="2 (default): the dense AdamW step; 1: the launch-bound small step; "
+                         "4: the hybrid Muon+AdamW step; 5: row-sparse AdamW on pinned-host state")
     ap.add_argument("--rounds", type=int, default=8, help="N > 1: update/all-gather rounds per step")
     ap.add_argument("--reserve-sms", type=int, default=24, help="N > 1: SMs left to NCCL during the update")
     ap.add_argument("--no-peer-writes", action="store_true",
@@ -1207,6 +1285,9 @@ def main():
         return
     if args.extra:
         run_extra(args)
+        return
+    if args.config == 1:
+        run_config1(args)
         return
     if args.config == 4 and (args.ns_shape or world == 1):
         run_ns_only(args) if args.ns_shape else run_config4(args)
