@@ -281,6 +281,8 @@ class AdamW(torch.optim.Optimizer):
         self.low_precision_copies: dict[torch.Tensor, torch.Tensor] = {}
         self._engine: StepEngine | None = None
         self._generation = 0
+        # per parameter, after its first step: (p, its state dict, copy, device, shape)
+        self._prepared: dict[int, tuple] = {}
 
     # -- helpers ---------------------------------------------------------------------
     def _engine_for(self, device) -> StepEngine:
@@ -321,34 +323,42 @@ class AdamW(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        entries, groups, gdt, device = [], [], None, None
+        entries, groups, gdt, device, last_dtype = [], [], None, None, None
+        prepared = self._prepared
         for gi, group in enumerate(self.param_groups):
             b1, b2 = group["betas"]
             groups.append((float(group["lr"]), float(b1), float(b2), float(group["eps"]),
                            float(group["weight_decay"]), "torch"))
             for p in group["params"]:
-                if p.grad is None:
-                    continue
                 g = p.grad
-                if not p.is_cuda or p.dtype != torch.float32 or not p.is_contiguous():
-                    raise ValueError("parameters must be contiguous float32 CUDA tensors")
-                if g.shape != p.shape or g.device != p.device or not g.is_contiguous():
+                if g is None:
+                    continue
+                ready = prepared.get(id(p))
+                if ready is None or ready[0] is not p:
+                    # first step of this parameter (or after a state change): validate, create state
+                    if not p.is_cuda or p.dtype != torch.float32 or not p.is_contiguous():
+                        raise ValueError("parameters must be contiguous float32 CUDA tensors")
+                    eng = self._engine_for(p.device)
+                    st = self._init_state(p, eng)
+                    out = None
+                    if self.low_precision is not None:
+                        out = self.low_precision_copies.get(p)
+                        if out is None:
+                            out = torch.empty_like(p, dtype=self.low_precision)
+                            self.low_precision_copies[p] = out
+                    ready = prepared[id(p)] = (p, st, out, p.device, p.shape)
+                if g.shape != ready[4] or g.device != ready[3] or not g.is_contiguous():
                     raise ValueError("gradient must be contiguous, on the parameter's device and shape")
-                code = _lib.dtype_code(g.dtype)
-                if gdt is None:
-                    gdt = code
-                elif code != gdt:
-                    raise ValueError("all gradients of one step must share a dtype")
-                device = p.device
-                eng = self._engine_for(p.device)
-                st = self._init_state(p, eng)
-                out = None
-                if self.low_precision is not None:
-                    out = self.low_precision_copies.get(p)
-                    if out is None:
-                        out = torch.empty_like(p, dtype=self.low_precision)
-                        self.low_precision_copies[p] = out
-                entries.append((p, st["exp_avg"], st["exp_avg_sq"], g, out, gi))
+                if g.dtype is not last_dtype:
+                    code = _lib.dtype_code(g.dtype)
+                    if gdt is None:
+                        gdt = code
+                    elif code != gdt:
+                        raise ValueError("all gradients of one step must share a dtype")
+                    last_dtype = g.dtype
+                device = ready[3]
+                st = ready[1]
+                entries.append((p, st["exp_avg"], st["exp_avg_sq"], g, ready[2], gi))
         if not entries:
             return loss
         eng = self._engine_for(device)
@@ -357,6 +367,7 @@ class AdamW(torch.optim.Optimizer):
                 if id(p) in eng.slots:
                     st["step"] = eng.clock_view(p)
             self._generation = eng.generation
+            self._prepared.clear()
         odt = _lib.dtype_code(self.low_precision) if self.low_precision is not None else _lib.MB_NONE
         with torch.cuda.device(device):
             eng.step(entries, groups, gdt, odt, self._fin_flags(), self.max_norm)
@@ -402,6 +413,7 @@ class AdamW(torch.optim.Optimizer):
         return sd
 
     def load_state_dict(self, state_dict):
+        self._prepared.clear()
         super().load_state_dict(state_dict)
         for group in self.param_groups:
             for p in group["params"]:
