@@ -325,6 +325,13 @@ MB_API int mb_offload_rows_step(float* host_w, float* host_m, float* host_v, int
                                 const mb_host_scalars* s, float* window0, float* window1, int64_t window_rows,
                                 mb_stream_t compute, mb_stream_t h2d, mb_stream_t d2h, int32_t* err_flag);
 
+/* Host wait with a bound (the "wait" of the reference's slot protocol,
+ * streamtrain/engine.py:111-112, which blocks without one): returns MB_OK once
+ * all work enqueued on `stream` has finished, MB_ERR_TIMEOUT when timeout_us
+ * elapses first (the work keeps running; call again to keep waiting), or
+ * MB_ERR_CUDA if the stream reported an error. Polls; never blocks the GPU. */
+MB_API int mb_stream_wait(mb_stream_t stream, int64_t timeout_us);
+
 /* Block-scaled FP8 transport (streamtrain/precision.py:24-37): per 256-element
  * block, scale = max(amax|x| / 448, 1e-30) and codes = e4m3fn(clamp(x / scale,
  * -448, 448)) (round to nearest even); codes has n bytes, scales

@@ -96,6 +96,7 @@ SIGNATURES = {
     "mb_fp8_unpack": (ctypes.c_int, [_p, _p, _i64, _p, _i32, _p]),
     "mb_offload_rows_step": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _p, _p, _p, _i64, _p, _p,
                                             _p, _p]),
+    "mb_stream_wait": (ctypes.c_int, [_p, _i64]),
     "mb_accumulate_workspace_bytes": (ctypes.c_size_t, []),
     "mb_grad_accumulate": (ctypes.c_int, [_p, _p, _i32, _i64, ctypes.c_float, _i32, _p, _p, _p]),
     "mb_export_f16": (ctypes.c_int, [_p, _i64, _p, _p, _p]),

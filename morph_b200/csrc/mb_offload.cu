@@ -23,7 +23,9 @@
 // caller that synchronises the compute stream sees the host state final.
 // The events are per device and reused: calls on one device must be issued
 // in order from one thread.
+#include <chrono>
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "mb_common.cuh"
@@ -147,6 +149,22 @@ MB_API int mb_offload_rows_step(float* host_w, float* host_m, float* host_v, int
   for (int b = 0; b < 2 && b < nwin; ++b)
     if (cudaStreamWaitEvent(sc, ev->scattered[b], 0) != cudaSuccess) return MB_ERR_CUDA;
   return MB_OK;
+}
+
+MB_API int mb_stream_wait(mb_stream_t stream, int64_t timeout_us) {
+  if (timeout_us < 0) return MB_ERR_ARG;
+  const auto t0 = std::chrono::steady_clock::now();
+  int64_t pause_us = 1;
+  while (true) {
+    const cudaError_t q = cudaStreamQuery((cudaStream_t)stream);
+    if (q == cudaSuccess) return MB_OK;
+    if (q != cudaErrorNotReady) return MB_ERR_CUDA;
+    const int64_t waited =
+        std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
+    if (waited >= timeout_us) return MB_ERR_TIMEOUT;
+    std::this_thread::sleep_for(std::chrono::microseconds(pause_us));
+    if (pause_us < 200) pause_us *= 2;  // poll densely at first, then every 0.2 ms
+  }
 }
 
 }  // extern "C"

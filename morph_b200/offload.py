@@ -57,9 +57,17 @@ class OffloadedRowTable:
                 _lib.stream_handle(self.h2d), _lib.stream_handle(self.d2h), _lib.ptr(self._err)),
                 "offload_rows_step")
 
-    def synchronize(self) -> None:
-        """Wait for every enqueued step; raise IndexError if an index was out of range."""
-        torch.cuda.current_stream(self.device).synchronize()
+    def synchronize(self, timeout: float | None = None) -> None:
+        """Wait for every enqueued step; raise IndexError if an index was out of
+        range. With ``timeout`` (seconds) the wait is bounded: TimeoutError is
+        raised if the steps have not finished by then (they keep running)."""
+        stream = torch.cuda.current_stream(self.device)
+        if timeout is None:
+            stream.synchronize()
+        else:
+            with torch.cuda.device(self.device):
+                _lib.check(_lib.lib().mb_stream_wait(_lib.stream_handle(stream), int(timeout * 1e6)),
+                           "offloaded rows still in flight")
         if int(self._err.item()):
             self._err.zero_()
             raise IndexError("row index out of range")
@@ -102,5 +110,5 @@ class ShardedRowTable:
             self.local.step(index[a:b] - self.lo, grads[a:b], step, lr, clip, loss_scale)
         return b - a
 
-    def synchronize(self) -> None:
-        self.local.synchronize()
+    def synchronize(self, timeout: float | None = None) -> None:
+        self.local.synchronize(timeout)

@@ -102,3 +102,20 @@ def test_row_sharded_two_gpus_equal_oracle(cuda):
         np.testing.assert_array_equal(wl, w[lo:hi])
         np.testing.assert_array_equal(ml, m[lo:hi])
     assert res[0][1] == res[1][0] and res[1][1] == rows
+
+
+def test_bounded_stream_wait(cuda):
+    """mb_stream_wait returns MB_ERR_TIMEOUT while work is still queued (the
+    work keeps running) and MB_OK once it has finished; the offload table's
+    synchronize(timeout=...) raises TimeoutError the same way."""
+    from morph_b200 import _lib
+    from morph_b200.offload import OffloadedRowTable
+    s = torch.cuda.current_stream(cuda)
+    torch.cuda._sleep(int(1.5e9))  # ~1 s of GPU time at B200 clocks (a bounded spin)
+    assert _lib.lib().mb_stream_wait(_lib.stream_handle(s), 1000) == _lib.MB_ERR_TIMEOUT
+    assert _lib.lib().mb_stream_wait(_lib.stream_handle(s), 30_000_000) == _lib.MB_OK
+    table = OffloadedRowTable(64, 8, device=cuda, window_bytes=2 * 3 * 8 * 4)
+    torch.cuda._sleep(int(1.5e9))
+    with pytest.raises(TimeoutError):
+        table.synchronize(timeout=1e-3)
+    table.synchronize(timeout=30.0)

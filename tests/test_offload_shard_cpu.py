@@ -24,7 +24,7 @@ class Recorder:
         assert index.dtype == torch.int64 and int(index.min()) >= 0 and int(index.max()) < self.rows
         self.calls.append((index.clone(), grads.clone(), step, lr, clip))
 
-    def synchronize(self):
+    def synchronize(self, timeout=None):
         pass
 
 
