@@ -20,6 +20,10 @@ Reference lines restated (paths inside the MORPH project):
   - ``clip_coef_disk``: streamtrain/disk.py:489.
   - ``orthogonalize``: streamtrain/optimizer.py:13-22.
   - ``partition``-independent Muon step: streamtrain/optimizer.py:52-61.
+  - ``grad_accumulate_``: streamtrain/sparse_disk.py:82-110 (window zeroed, then
+    ``destination.add_(g.float() / loss_scale)`` per microbatch).
+  - ``export_f16_chunks``: streamtrain/export.py:30-35 (chunked check and cast).
+  - ``pack_fp8`` / ``unpack_fp8``: streamtrain/precision.py:20-37.
 
 Parity pin: tests/test_oracle_cpu.py checks this oracle against golden vectors
 produced by running the reference itself (tests/golden/make_golden.py) and
