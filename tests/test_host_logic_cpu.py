@@ -1,0 +1,83 @@
+"""Host-side logic that needs no GPU: the bias-correction tables, the disk-rule
+step scalars, the Muon batch plan and operand choice, and the library's
+workspace sizing (host-only C-ABI entry points)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from morph_b200 import _lib
+from oracle import oracle as orc
+
+
+def test_bias_correction_tables_match_the_reference_expressions():
+    from morph_b200.optim import BiasCorrectionTables
+    t = BiasCorrectionTables("cpu")
+    t.index(.9, .999, "torch")
+    t.index(.9, .95, "torch")
+    t.index(.9, .999, "disk")
+    tab, n = t.ensure(1)
+    assert n == math.ceil(60 * math.log(2) / -math.log(.999)) + 2  # built to saturation up front
+    tab = tab.numpy()
+    for step in (1, 2, 3, 100, 1023, 5000, 41000):
+        assert tab[0, step] == 1 - .9 ** float(step)
+        assert tab[1, step] == (1 - .999 ** float(step)) ** 0.5
+        assert tab[3, step] == (1 - .95 ** float(step)) ** 0.5
+        assert tab[5, step] == math.sqrt(1 - .999 ** float(step))
+    assert tab[1, n - 1] == 1.0 and tab[0, n - 1] == 1.0  # saturated: clocks beyond clamp exactly
+    again, n2 = t.ensure(10 ** 6)
+    assert again is t.tensor and n2 == n  # never rebuilt once saturated
+
+
+def test_bias_correction_tables_are_bounded_for_beta2_near_one():
+    from morph_b200.optim import BiasCorrectionTables
+    t = BiasCorrectionTables("cpu")
+    t.index(.9, .999999, "torch")
+    _, n = t.ensure(1)
+    assert n == BiasCorrectionTables.MAX_LENGTH
+
+
+@pytest.mark.parametrize("lr,step,clip,scale", [(1e-4, 1, 1.0, 1.0), (3e-3, 7, .25, 1024.0), (1e-3, 41000, .5, 3.0)])
+def test_disk_host_scalars_match_the_oracle(lr, step, clip, scale):
+    from morph_b200.disk import disk_host_scalars
+    s = disk_host_scalars(lr, step, clip, scale)
+    o = orc.disk_scalars(lr, step)
+    for ours, theirs in (("cwd", "cwd"), ("omb1", "omb1"), ("beta2", "b2"), ("omb2", "omb2"), ("bc2s", "bc2s"),
+                         ("eps", "eps"), ("nss", "nss")):
+        assert getattr(s, ours) == getattr(o, theirs), ours
+    assert s.scale == np.float32(scale) and s.coef == np.float32(clip)
+
+
+def test_muon_batch_plan_and_operands():
+    from morph_b200.muon import batch_plan, ns_operand_dtype
+    per = _lib.lib().mb_muon_batch_workspace_bytes(1, 4096, 11008)
+    assert per > 0 and _lib.lib().mb_muon_batch_workspace_bytes(2, 4096, 11008) > per
+    for count in (1, 7, 96, 128, 200):
+        for limit in (1, per * 5, 4 << 30):
+            sizes = batch_plan(count, 4096, 11008, limit)
+            assert sum(sizes) == count
+            assert max(sizes) <= max(1, min(_lib.MB_MUON_MAX_BATCH, limit // per))
+            assert all(x == sizes[0] for x in sizes[:-1]) and sizes[-1] <= sizes[0]  # evenly filled
+    assert batch_plan(0, 64, 64, 1 << 30) == []
+    with pytest.raises(ValueError):
+        batch_plan(3, 0, 64, 1 << 30)
+    assert ns_operand_dtype(48, 80) == _lib.MB_F16 and ns_operand_dtype(4096, 4096, "bf16") == _lib.MB_BF16
+    with pytest.raises(ValueError):
+        ns_operand_dtype(64, 64, "fp8")
+
+
+def test_workspace_sizes_are_aligned_and_grow():
+    L = _lib.lib()
+    sizes = [L.mb_workspace_bytes(n) for n in (1, 2, 100, 8192)]
+    assert all(s % 256 == 0 for s in sizes) and sizes == sorted(sizes)
+    assert L.mb_accumulate_workspace_bytes() >= 8 * 1024
+    assert L.mb_muon_workspace_bytes(0, 64) == 0 and L.mb_muon_workspace_bytes(64, 64) > 0
+
+
+def test_dtype_codes_and_status_mapping():
+    assert _lib.dtype_code(torch.bfloat16) == _lib.MB_BF16 and _lib.dtype_code(None) == _lib.MB_NONE
+    with pytest.raises(ValueError):
+        _lib.dtype_code(torch.int8)
+    with pytest.raises(TimeoutError):
+        _lib.check(_lib.MB_ERR_TIMEOUT)
