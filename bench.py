@@ -1022,8 +1022,10 @@ def run_morph_zero(args, rank, world, local_rank):
     for (_, shape), n in zip(shapes, sizes):
         params.append(full[off:off + n].view(shape))
         off += n
+    # sync=False: step() only enqueues, as the one-GPU run's AdamW does; a refused
+    # step is reported by last_step() after the timed region
     opt = ZeroAdamW(params, LR, BETAS, EPS, WD, max_norm=MAX_NORM, gate=True, device=device, rounds=args.rounds,
-                    reserve_sms=args.reserve_sms, peer_writes=False if args.no_peer_writes else "auto")
+                    reserve_sms=args.reserve_sms, peer_writes=False if args.no_peer_writes else "auto", sync=False)
     del params, full
     torch.cuda.empty_cache()
     gflat = torch.empty(total, dtype=torch.bfloat16, device=device)

@@ -196,11 +196,17 @@ class ZeroAdamW:
     ``step(grads)`` the full updated weights are in ``weights`` (one
     low-precision tensor per parameter, views of one flat buffer). ``rounds``
     is the number of update/all-gather rounds that overlap (1 on one GPU);
-    ``reserve_sms`` SMs are left free of kernel 1 for NCCL's all-gather."""
+    ``reserve_sms`` SMs are left free of kernel 1 for NCCL's all-gather.
+
+    ``sync`` (default: ``gate``) makes ``step`` wait for the step's device
+    record and raise FloatingPointError at once when the gate refused it.
+    With ``sync=False`` the step only enqueues work, so the host prepares the
+    next step while this one runs; a refused step still changes nothing on
+    any rank, and ``check()`` (or ``last_step()``) reports it later."""
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-2, *, max_norm=None,
                  clip_mode="torch", gate=False, low_precision=torch.bfloat16, process_group=None, device=None,
-                 backend=None, rounds=8, reserve_sms=24, peer_writes="auto"):
+                 backend=None, rounds=8, reserve_sms=24, peer_writes="auto", sync=None):
         params = list(params)
         if not params:
             raise ValueError("ZeroAdamW needs parameters")
@@ -210,6 +216,7 @@ class ZeroAdamW:
         self.device = torch.device(device) if device is not None else params[0].device
         self.lr, self.betas, self.eps, self.weight_decay = lr, tuple(betas), eps, weight_decay
         self.max_norm, self.clip_mode, self.gate = max_norm, clip_mode, gate
+        self.sync = gate if sync is None else bool(sync)
         if clip_mode not in ("torch", "disk"):
             raise ValueError("clip_mode must be 'torch' or 'disk'")
         self.low_precision = low_precision
@@ -349,10 +356,14 @@ class ZeroAdamW:
             dist.all_reduce(self._done, group=self.group)
         if events:
             events[3].record()
-        if self.gate:
-            info = self.backend.last_step()
-            if info["status"]:
-                _lib.check(info["status"], "optimizer not updated")
+        if self.sync:
+            self.check()
+
+    def check(self) -> None:
+        """Wait for the last step and raise FloatingPointError if it was refused."""
+        info = self.backend.last_step()
+        if info["status"]:
+            _lib.check(info["status"], "optimizer not updated")
 
     def last_step(self) -> dict:
         return self.backend.last_step()

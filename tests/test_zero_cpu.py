@@ -151,3 +151,29 @@ def test_two_gloo_ranks_equal_one_rank():
     torch.testing.assert_close(masters, single[0], rtol=1e-6, atol=1e-6 * LR)
     assert torch.equal(full0, full1)  # both ranks hold the same gathered weights
     torch.testing.assert_close(full0.float(), single[1].float(), rtol=1e-2, atol=0)
+
+
+@pytest.mark.parametrize("sync", [None, False])
+def test_refused_step_changes_nothing_and_raises(sync):
+    """gate: a nonfinite gradient leaves masters and weights unchanged. The
+    default (sync=gate) raises FloatingPointError inside step(); sync=False only
+    enqueues the step and check() raises afterwards."""
+    params, grads = _inputs()
+    opt = ZeroAdamW(params, LR, BETAS, EPS, WD, max_norm=1.0, gate=True, device="cpu", backend=OracleBackend(1.0),
+                    rounds=2, sync=sync)
+    opt.step(grads[0])
+    master, weights = opt.master.clone(), opt.flat_weights.clone()
+    bad = [g.clone() for g in grads[1]]
+    bad[2][5, 7] = float("inf")
+    if sync is None:
+        with pytest.raises(FloatingPointError):
+            opt.step(bad)
+    else:
+        opt.step(bad)
+        assert opt.last_step()["skipped"]
+        with pytest.raises(FloatingPointError):
+            opt.check()
+    assert torch.equal(opt.master, master) and torch.equal(opt.flat_weights, weights)
+    opt.step(grads[2])  # the next finite step proceeds
+    opt.check()
+    assert not torch.equal(opt.master, master)
