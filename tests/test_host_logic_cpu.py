@@ -81,3 +81,37 @@ def test_dtype_codes_and_status_mapping():
         _lib.dtype_code(torch.int8)
     with pytest.raises(TimeoutError):
         _lib.check(_lib.MB_ERR_TIMEOUT)
+
+
+def test_partition_follows_the_reference_rule():
+    """streamtrain/optimizer.py:25-31: the weight of every nn.Linear whose
+    module name is not exactly 'lm_head' goes to Muon; biases, embeddings,
+    norms, the top-level lm_head and anything else go to AdamW, both lists in
+    model.parameters() order (tied parameters once)."""
+    from morph_b200.muon import partition
+
+    class Block(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.up = torch.nn.Linear(4, 8)
+            self.down = torch.nn.Linear(8, 4, bias=False)
+            self.norm = torch.nn.LayerNorm(4)
+            self.lm_head = torch.nn.Linear(4, 4, bias=False)  # nested: its name is 'blocks.0.lm_head'
+
+    class Model(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.embed = torch.nn.Embedding(10, 4)
+            self.blocks = torch.nn.ModuleList([Block(), Block()])
+            self.lm_head = torch.nn.Linear(4, 10, bias=False)
+            self.lm_head.weight = self.embed.weight  # tied
+
+    model = Model()
+    muon, adam = partition(model)
+    want_muon = [b.up.weight for b in model.blocks] + [b.down.weight for b in model.blocks] + \
+                [b.lm_head.weight for b in model.blocks]
+    assert {id(p) for p in muon} == {id(p) for p in want_muon} and len(muon) == len(want_muon)
+    order = [id(p) for p in model.parameters()]
+    assert [id(p) for p in muon] == sorted((id(p) for p in muon), key=order.index)
+    assert [id(p) for p in adam] == [i for i in order if i not in {id(p) for p in muon}]
+    assert id(model.embed.weight) in {id(p) for p in adam}
