@@ -234,7 +234,10 @@ MB_API int mb_adamw_update(float* w, float* m, float* v, const void* g, int32_t 
 /* Kernel 3: lazy row-sparse AdamW. Rows idx[0..k) of the [rows, cols] FP32
  * planes w, m, v take one step with gradient row r = grads[r*cols ..]. Rows not
  * listed are not read or written. An index outside [0, rows) is skipped and
- * sets *err_flag (device int32, may be NULL) to 1. cols must be a multiple of 4. */
+ * sets *err_flag (device int32, may be NULL) to 1. Each row is listed at most
+ * once (the reference's sorted, unique index sets); a row listed twice is
+ * updated by two CTAs at once, in no defined order. Any cols >= 1 works; cols
+ * a multiple of 4 with 16-byte aligned planes and gradients takes the vector path. */
 MB_API int mb_sparse_rows_update(float* w, float* m, float* v, int64_t rows, int64_t cols,
                                  const int64_t* idx, int64_t k, const void* grads,
                                  int32_t grad_dtype, const mb_host_scalars* s,
