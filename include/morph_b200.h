@@ -3,9 +3,10 @@
  *
  * Every entry point takes raw device pointers, element counts, dtype codes and
  * a CUDA stream, returns an int status (MB_OK = 0) and throws nothing. No entry
- * point allocates parameter memory or synchronises the host with the device;
- * callers own every buffer (state, workspace, tables) and size the workspace
- * with mb_workspace_bytes().
+ * point allocates parameter memory or synchronises the host with the device,
+ * except the two whose job that is: mb_ipc_alloc (peer-mapped buffers) and
+ * mb_stream_wait (a bounded host wait). Callers own every buffer (state,
+ * workspace, tables) and size the workspace with mb_workspace_bytes().
  *
  * Reference interfaces replaced (paths inside the everett6/MORPH project):
  *   mb_adamw_step / mb_grad_stats / mb_step_finalize / mb_adamw_apply
