@@ -265,14 +265,14 @@ class ZeroAdamW:
     def _want_peers(self, peer_writes, backend):
         """Fused update + all-gather (kernel 1 stores the low-precision copies
         into every rank's buffer over NVLink) when the ranks share a node."""
+        if peer_writes is not True and peer_writes is not False and peer_writes != "auto":
+            raise ValueError("peer_writes must be True, False or 'auto'")
         if self.world == 1 or backend is not None or self.low_precision not in (torch.bfloat16, torch.float16):
             if peer_writes is True:
                 raise ValueError("peer writes need several ranks, the CUDA backend and a 16-bit copy")
             return False
-        if peer_writes in (True, False):
-            return peer_writes
         if peer_writes != "auto":
-            raise ValueError("peer_writes must be True, False or 'auto'")
+            return peer_writes
         import socket
         hosts = [None] * self.world
         dist.all_gather_object(hosts, socket.gethostname(), group=self.group)

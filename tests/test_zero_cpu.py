@@ -177,3 +177,15 @@ def test_refused_step_changes_nothing_and_raises(sync):
     opt.step(grads[2])  # the next finite step proceeds
     opt.check()
     assert not torch.equal(opt.master, master)
+
+
+def test_peer_writes_need_the_cuda_backend_and_several_ranks():
+    """Peer stores are a CUDA-IPC path: asking for them with another backend
+    (or on one rank) is an error; "auto" quietly falls back to the NCCL rounds."""
+    params, _ = _inputs()
+    with pytest.raises(ValueError):
+        ZeroAdamW(params, LR, BETAS, EPS, WD, device="cpu", backend=OracleBackend(None), peer_writes=True)
+    opt = ZeroAdamW(params, LR, BETAS, EPS, WD, device="cpu", backend=OracleBackend(None), peer_writes="auto")
+    assert opt.peer_writes is False and opt.rounds == 1  # one rank: one round
+    with pytest.raises(ValueError):
+        ZeroAdamW(params, LR, BETAS, EPS, WD, device="cpu", backend=OracleBackend(None), peer_writes="yes")
