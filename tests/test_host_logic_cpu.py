@@ -115,3 +115,26 @@ def test_partition_follows_the_reference_rule():
     assert [id(p) for p in muon] == sorted((id(p) for p in muon), key=order.index)
     assert [id(p) for p in adam] == [i for i in order if i not in {id(p) for p in muon}]
     assert id(model.embed.weight) in {id(p) for p in adam}
+
+
+def test_adamw_constructor_rejects_what_torch_rejects():
+    """morph_b200.AdamW raises where torch.optim.AdamW does (lr, eps, betas) and
+    refuses the torch options the kernels do not implement."""
+    from morph_b200 import AdamW
+    ps = [torch.nn.Parameter(torch.zeros(4))]
+    for kw in (dict(lr=-1e-3), dict(eps=-1.0), dict(betas=(1.0, .999)), dict(betas=(.9, -0.1))):
+        with pytest.raises(ValueError):
+            torch.optim.AdamW(ps, **kw)
+        with pytest.raises(ValueError):
+            AdamW(ps, **kw)
+    for kw in (dict(amsgrad=True), dict(maximize=True), dict(differentiable=True)):
+        with pytest.raises(NotImplementedError):
+            AdamW(ps, **kw)
+    with pytest.raises(ValueError):
+        AdamW(ps, clip_mode="other")
+    opt = AdamW(ps, lr=3e-4, betas=(.9, .95), weight_decay=.1)
+    ref = torch.optim.AdamW(ps, lr=3e-4, betas=(.9, .95), weight_decay=.1, foreach=False)
+    assert set(opt.param_groups[0]) >= {"lr", "betas", "eps", "weight_decay", "amsgrad", "maximize", "foreach",
+                                       "capturable", "differentiable", "fused"}
+    for k in ("lr", "betas", "eps", "weight_decay", "amsgrad", "maximize"):
+        assert opt.param_groups[0][k] == ref.param_groups[0][k], k
