@@ -138,3 +138,32 @@ def test_adamw_constructor_rejects_what_torch_rejects():
                                        "capturable", "differentiable", "fused"}
     for k in ("lr", "betas", "eps", "weight_decay", "amsgrad", "maximize"):
         assert opt.param_groups[0][k] == ref.param_groups[0][k], k
+
+
+def test_loss_scale_host_transitions_follow_the_reference():
+    """morph_b200.DynamicLossScale's host-driven overflow()/success() and
+    state_dict round trip, on a host-resident record, step for step against the
+    restatement of streamtrain/precision.py:6-17 (pinned to the reference's
+    golden sequences in test_oracle_cpu.py)."""
+    from morph_b200 import DynamicLossScale
+    assert DynamicLossScale(device="cpu").scale == 128.0  # precision.py:7 default
+    for scale, interval in ((128., 2000), (4., 3), (32768., 2), (1., 1)):
+        ours, ref = DynamicLossScale(scale, interval, device="cpu"), orc.DynamicLossScale(scale, interval)
+        rng = np.random.default_rng(int(scale) + interval)
+        for _ in range(40):
+            if rng.random() < .3:
+                raised = []
+                for s in (ours, ref):
+                    try:
+                        s.overflow()
+                        raised.append(False)
+                    except FloatingPointError:
+                        raised.append(True)
+                assert raised[0] == raised[1]
+            else:
+                ours.success()
+                ref.success()
+            assert ours.state_dict() == ref.state_dict()
+        other = DynamicLossScale(device="cpu")
+        other.load_state_dict(ours.state_dict())
+        assert other.state_dict() == ours.state_dict()
