@@ -1,6 +1,7 @@
 """Host-side logic that needs no GPU: the bias-correction tables, the disk-rule
-step scalars, the Muon batch plan and operand choice, and the library's
-workspace sizing (host-only C-ABI entry points)."""
+step scalars, the Muon batch plan and operand choice, the library's workspace
+sizing (host-only C-ABI entry points), the Muon/AdamW partition, the AdamW
+constructor's validation and the loss scale's host transitions."""
 import math
 
 import numpy as np
