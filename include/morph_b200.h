@@ -212,9 +212,12 @@ MB_API int mb_ipc_close(void* ptr);
  * plan->workspace is ignored and may be NULL: the kernels use one fixed
  * library-owned device array instead (about 129 KiB per GPU, held until exit).
  * At most 8192 segments; larger plans return MB_ERR_TOO_LARGE and nothing runs.
- * The first call on a device looks the array up (cudaGetSymbolAddress): make it
- * before any stream capture. Calls share the array; calls that may overlap on
- * the GPU race, so order them on one stream. Allocates nothing. */
+ * fin is required (NULL returns MB_ERR_ARG). The plan and fin are validated
+ * before anything is queued. The first call on a device looks the array up
+ * (cudaGetSymbolAddress) and caches it for the current CUDA context (a new
+ * context, e.g. after cudaDeviceReset, is looked up again): make that first
+ * call before any stream capture. Calls share the array; calls that may
+ * overlap on the GPU race, so order them on one stream. Allocates nothing. */
 MB_API int mb_adamw_step_noalloc(const mb_adamw_plan* plan, const mb_finalize_opts* fin, mb_stream_t stream);
 
 /* --------------------------------------- single tensor, host scalars -- */

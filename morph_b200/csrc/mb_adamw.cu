@@ -933,6 +933,10 @@ StatsFn pick_stats(int gdt, bool unscale) {
   }
 }
 
+int launch_status() { return cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA; }
+
+}  // namespace
+
 int check_plan(const mb_adamw_plan* p) {
   if (!p || !p->segs || !p->groups || !p->bc || !p->clocks || !p->workspace || !p->state) return MB_ERR_ARG;
   if (p->n_segs <= 0 || p->n_groups <= 0 || p->n_tiles <= 0 || p->bc_len <= 0) return MB_ERR_ARG;
@@ -951,9 +955,6 @@ int check_fin(const mb_finalize_opts* f) {
   return MB_OK;
 }
 
-int launch_status() { return cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA; }
-
-}  // namespace
 }  // namespace mb
 
 using namespace mb;

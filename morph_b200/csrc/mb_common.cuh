@@ -240,6 +240,11 @@ struct GemmCall {
 };
 int gemm16(const GemmCall& call, cudaStream_t stream);
 
+// Host-side validation of a fused AdamW plan and of finalize options (MB_OK or
+// the status the entry points return).
+int check_plan(const mb_adamw_plan* p);
+int check_fin(const mb_finalize_opts* f);
+
 // Number of CTAs a persistent streaming kernel launches on the current device.
 int persistent_blocks(const void* kernel, int threads, size_t smem);
 // Persistent grid for `fn` (kThreads threads), capped at n_tiles; cached per device.

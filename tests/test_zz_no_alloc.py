@@ -70,6 +70,54 @@ def test_noalloc_step_matches_allocating_step_on_two_calls(cuda):
     assert sb.clip_coef < 1.0  # the second call's gradients were clipped
 
 
+def test_noalloc_takes_a_plan_at_its_segment_limit(cuda):
+    """8192 segments (the scratch's capacity) run, and equal mb_adamw_step."""
+    from morph_b200 import _lib
+    from morph_b200.optim import StepEngine
+    L = _lib.lib()
+    n_segs = 8192
+    sizes = [1 + (i * 7) % 13 for i in range(n_segs)]  # ragged, tiny segments
+    n = sum(sizes)
+    runs = []
+    for _ in range(2):
+        gen = torch.Generator(device=cuda).manual_seed(3)
+        w = torch.randn(n, device=cuda, generator=gen) * 0.02
+        m, v = torch.zeros_like(w), torch.zeros_like(w)
+        g = (torch.randn(n, device=cuda, generator=gen) * 1e-3).to(torch.bfloat16)
+        eng = StepEngine(cuda)
+        entries, off = [], 0
+        for s in sizes:
+            piece = w[off:off + s]
+            eng.slot(piece, 0)
+            entries.append((piece, m[off:off + s], v[off:off + s], g[off:off + s], None, 0))
+            off += s
+        plan = eng.prepare(entries, [(3e-4, .9, .95, 1e-8, .1, "torch")], _lib.MB_BF16, _lib.MB_NONE)
+        fin = eng.finalize_opts(_lib.MB_FIN_CLIP_TORCH | _lib.MB_FIN_GATE, 1.0)
+        runs.append((eng, plan, fin, w, m, v, entries))
+    (ea, pa, fa, wa, ma, va, _), (eb, pb, fb, wb, mb, vb, _) = runs
+    pb.workspace = None
+    stream = _lib.stream_handle()
+    _lib.check(L.mb_adamw_step(ctypes.byref(pa), ctypes.byref(fa), stream))
+    assert L.mb_adamw_step_noalloc(ctypes.byref(pb), ctypes.byref(fb), stream) == _lib.MB_OK
+    torch.cuda.synchronize()
+    assert torch.equal(wa, wb) and torch.equal(ma, mb) and torch.equal(va, vb)
+    assert torch.equal(ea.clocks, eb.clocks) and int(eb.clocks[n_segs - 1]) == 1
+
+
+def test_noalloc_requires_finalize_options(cuda):
+    """fin = NULL is refused before anything is queued (mb_adamw_step would
+    accept it and skip the finalize)."""
+    from morph_b200 import _lib
+    L = _lib.lib()
+    a = _setup(cuda, 5)
+    a["plan"].workspace = None
+    w0 = a["w"].clone()
+    rc = L.mb_adamw_step_noalloc(ctypes.byref(a["plan"]), None, _lib.stream_handle())
+    assert rc == _lib.MB_ERR_ARG
+    torch.cuda.synchronize()
+    assert torch.equal(a["w"], w0) and int(a["eng"].clocks[0]) == 0
+
+
 def test_noalloc_rejects_plans_beyond_its_scratch(cuda):
     from morph_b200 import _lib
     L = _lib.lib()
