@@ -220,6 +220,20 @@ MB_API int mb_ipc_close(void* ptr);
  * overlap on the GPU race, so order them on one stream. Allocates nothing. */
 MB_API int mb_adamw_step_noalloc(const mb_adamw_plan* plan, const mb_finalize_opts* fin, mb_stream_t stream);
 
+/* Test-only, no counterpart in the reference: arms a fault for the next launch
+ * in this process of one kernel whose waits are bounded, so a test can make a
+ * bounded device wait expire without faulting anything. That launch withholds
+ * one unit's copy (kernel 1 = MB_FAULT_APPLY: the bulk-staged update's tile
+ * `unit`; MB_FAULT_STATS: the bulk-staged statistics pass's chunk starting at
+ * tile `unit`; MB_FAULT_GEMM: the first k-block of output tile `unit` of the
+ * kernel-4 GEMM) and bounds every wait of the launch by wait_limit_ns (1 us to
+ * 2 s). The consumers' wait for that unit expires; the CTA stops, drains its own
+ * copies in flight (bounded), frees what it holds and reports MB_ERR_TIMEOUT in
+ * the step state (kernel 2: the step is refused, nothing changes) or raises the
+ * GEMM's error flag. One arm is consumed by one launch; kernel 0 disarms all. */
+enum { MB_FAULT_APPLY = 1, MB_FAULT_STATS = 2, MB_FAULT_GEMM = 4 };
+MB_API int mb_debug_arm_fault(int32_t kernel, int64_t unit, int64_t wait_limit_ns);
+
 /* --------------------------------------- single tensor, host scalars -- */
 
 /* Step scalars computed on the host (float32 roundings of the reference's
@@ -275,6 +289,9 @@ typedef struct mb_muon_args {
   float cwd;         /* (float)(1 - lr * weight_decay)          */
   float neg_lr;      /* (float)(-lr)                            */
   int32_t ns_dtype;  /* Newton-Schulz operands: MB_BF16 or MB_F16 */
+  const int32_t* skip; /* optional device flag (e.g. &mb_step_state.skip of a gate
+                          finalized earlier on the stream): nonzero = every launch
+                          of the step returns at once and nothing changes */
 } mb_muon_args;
 
 /* Most matrices one mb_muon_step_batched call takes. */

@@ -25,6 +25,8 @@ MB_ERR_TOO_LARGE = 9
 MB_F32, MB_F16, MB_BF16, MB_NONE = 0, 1, 2, 3
 MB_MUON_MAX_BATCH = 64
 
+MB_FAULT_APPLY, MB_FAULT_STATS, MB_FAULT_GEMM = 1, 2, 4
+
 MB_FIN_LOSS_SCALE = 1
 MB_FIN_GATE = 2
 MB_FIN_CLIP_TORCH = 4
@@ -66,7 +68,8 @@ class Plan(ctypes.Structure):
 
 class MuonArgs(ctypes.Structure):
     _fields_ = [("beta_lerp", _f), ("nesterov", _f), ("ns_a", _f), ("ns_b", _f), ("ns_c", _f),
-                ("ns_steps", _i32), ("shape_scale", _f), ("cwd", _f), ("neg_lr", _f), ("ns_dtype", _i32)]
+                ("ns_steps", _i32), ("shape_scale", _f), ("cwd", _f), ("neg_lr", _f), ("ns_dtype", _i32),
+                ("skip", _p)]
 
 
 class HostScalars(ctypes.Structure):
@@ -111,6 +114,7 @@ SIGNATURES = {
     "mb_muon_step": (ctypes.c_int, [_p, _p, _p, _i32, _p, _i32, _i64, _i64, _p, _p, ctypes.c_size_t, _p, _p]),
     "mb_muon_step_batched": (ctypes.c_int, [_p, _p, _p, _i32, _p, _i32, _i32, _i64, _i64, _p, _p, ctypes.c_size_t,
                                             _p, _p]),
+    "mb_debug_arm_fault": (ctypes.c_int, [_i32, _i64, _i64]),
     "mb_gemm16": (ctypes.c_int, [_i32, _p, _i64, _p, _i64, _i64, _i64, _i64, _f, _f, _p, _i64, _p, _i64, _p, _i64,
                                  _p, _i64, _p, _p]),
 }

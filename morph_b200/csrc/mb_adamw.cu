@@ -76,6 +76,7 @@ struct ApplyArgs {
   // bytes (the peers' buffers mapped into this process).
   int32_t n_peers;
   int64_t peer_delta[kMaxPeers];
+  FaultPlan fault;  // test-only (bulk kernel): a withheld tile and the launch's wait bound
 };
 
 __device__ __forceinline__ StepScalars group_scalars(const mb_group& g, float2 ss) {
@@ -214,6 +215,9 @@ __global__ void __launch_bounds__(kThreads, MB_APPLY_MIN_BLOCKS) k_adamw_apply(A
 #ifndef MB_BULK_CTAS
 #define MB_BULK_CTAS 2
 #endif
+#ifndef MB_BULK_L2_HINT
+#define MB_BULK_L2_HINT 0  // 1: the producer's copies carry an L2 evict-first policy
+#endif
 constexpr int kBulkStages = MB_BULK_STAGES;        // ring depth (tiles)
 constexpr int kBulkConsumerWarps = MB_BULK_WARPS;  // consumers; each thread takes kBulkQuads quads of a tile
 constexpr int kBulkCtasPerSm = MB_BULK_CTAS;
@@ -282,7 +286,8 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkCtasPerSm) k_adamw_apply_bu
       for (int64_t tile = a.tile_lo + blockIdx.x; tile < a.n_tiles; tile += gridDim.x, ++k) {
         if (sc_.advance(a, tile)) seg = a.segs[sc_.cur];
         const int s = k % kBulkStages;
-        if (!mbar_wait(&empty[s], ((k / kBulkStages) & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(&empty[s], ((k / kBulkStages) & 1) ^ 1, abort_flag, a.fault.limit_ns)) break;
+        if (tile == a.fault.unit) continue;  // test-only: withhold this tile; its consumers' wait expires
         const int64_t t = tile - seg.tile_begin;
         const int64_t e = t * kTile;
         const int64_t rest = seg.numel - e;
@@ -290,10 +295,18 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkCtasPerSm) k_adamw_apply_bu
         if (bulk_ok(seg, GDT, ODT, n)) {
           uint8_t* base = smem + s * STAGE;
           mbar_expect_tx(&full[s], (uint32_t)n * (12 + GB));
+#if MB_BULK_L2_HINT
+          const uint64_t pol = l2_evict_first();
+          bulk_load_hint(base, seg.w + e, n * 4, &full[s], pol);
+          bulk_load_hint(base + kTile * 4, seg.m + e, n * 4, &full[s], pol);
+          bulk_load_hint(base + kTile * 8, seg.v + e, n * 4, &full[s], pol);
+          bulk_load_hint(base + kTile * 12, static_cast<const uint8_t*>(seg.g) + e * GB, n * GB, &full[s], pol);
+#else
           bulk_load(base, seg.w + e, n * 4, &full[s]);
           bulk_load(base + kTile * 4, seg.m + e, n * 4, &full[s]);
           bulk_load(base + kTile * 8, seg.v + e, n * 4, &full[s]);
           bulk_load(base + kTile * 12, static_cast<const uint8_t*>(seg.g) + e * GB, n * GB, &full[s]);
+#endif
           last_bulk[s] = k;
         } else {
           mbar_arrive(&full[s]);
@@ -306,7 +319,7 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkCtasPerSm) k_adamw_apply_bu
           if (last_bulk[i] < 0) continue;
           const uint32_t parity = (last_bulk[i] / kBulkStages) & 1;
           const uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(&full[i], parity) && globaltimer() - t0 < kWaitLimitNs) {
+          while (!mbar_try_wait(&full[i], parity) && globaltimer() - t0 < a.fault.limit_ns) {
           }
         }
       }
@@ -324,7 +337,7 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkCtasPerSm) k_adamw_apply_bu
         sc = group_scalars(a.groups[seg.group], a.seg_scal[sc_.cur]);
       }
       const int s = k % kBulkStages;
-      if (!mbar_wait(&full[s], (k / kBulkStages) & 1, abort_flag)) break;
+      if (!mbar_wait(&full[s], (k / kBulkStages) & 1, abort_flag, a.fault.limit_ns)) break;
       const int64_t t = tile - seg.tile_begin;
       const int64_t e = t * kTile;
       const int64_t rest = seg.numel - e;
@@ -415,7 +428,13 @@ struct StatsArgs {
   mb_finalize_opts fin;
   int32_t fuse_finalize;
   int32_t unscale;         // divide by state.scale
+  FaultPlan fault;         // test-only (bulk kernel): a withheld chunk and the launch's wait bound
 };
+
+// A CTA of kernel 2 whose bounded wait expired reports this many nonfinite
+// elements; the finalize reads any count at or above it as a time-out (sums of
+// real counts over ranks stay far below it).
+constexpr double kTimeoutMark = 1099511627776.0;  // 2^40
 
 // Block-wide sum of (a, b) in a fixed order; result valid in thread 0. Any
 // block size that is a multiple of 32, up to 1024.
@@ -452,7 +471,10 @@ __device__ void finalize_block(const mb_adamw_plan& p, const mb_finalize_opts& f
     bool found = st->nonfinite != 0.0 || !isfinite(sumsq);
     int skip = 0, status = MB_OK;
     double used = (f.flags & MB_FIN_LOSS_SCALE) ? st->scale : 1.0;
-    if (f.flags & MB_FIN_LOSS_SCALE) {
+    if (st->nonfinite >= kTimeoutMark) {
+      skip = 1;  // the statistics pass gave up: no norm, no update, loss scale unchanged
+      status = MB_ERR_TIMEOUT;
+    } else if (f.flags & MB_FIN_LOSS_SCALE) {
       if (found) {
         skip = 1;
         if (st->scale <= 1.0) {
@@ -551,7 +573,7 @@ __device__ __forceinline__ void stats_elems(const uint4& q, bool unscale, const 
 
 // Per-CTA partial {sum of squares, nonfinite} of kernel 2, the last CTA's
 // fixed-order reduction into the step state, and the optional fused finalize.
-__device__ void stats_tail(const StatsArgs& a, double acc) {
+__device__ void stats_tail(const StatsArgs& a, double acc, bool aborted = false) {
   mb_step_state* st = a.plan.state;
   double2 r = block_sum2(acc, 0.0);
   char* ws = static_cast<char*>(a.plan.workspace);
@@ -559,7 +581,7 @@ __device__ void stats_tail(const StatsArgs& a, double acc) {
   unsigned int* ticket = reinterpret_cast<unsigned int*>(ws + kTicketOffset);
   __shared__ unsigned int s_last;
   if (threadIdx.x == 0) {
-    r.y = isfinite(r.x) ? 0.0 : 1.0;
+    r.y = aborted ? kTimeoutMark : (isfinite(r.x) ? 0.0 : 1.0);
     partials[blockIdx.x] = r;
     __threadfence();
     s_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
@@ -735,9 +757,11 @@ __global__ void __launch_bounds__(kSBThreads) k_grad_stats_bulk(StatsArgs a) {
       for (int i = 0; i < kSBStages; ++i) last_bulk[i] = -1;
       for (int64_t t = t0; t < t1; ++k) {
         const StatsChunk c = stats_chunk<GDT>(a, cur, seg, t, t1);
+        const int64_t first = t;
         t += c.tiles;
         const int s = k % kSBStages;
-        if (!mbar_wait(&empty[s], ((k / kSBStages) & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(&empty[s], ((k / kSBStages) & 1) ^ 1, abort_flag, a.fault.limit_ns)) break;
+        if (first == a.fault.unit) continue;  // test-only: withhold this chunk; its consumers' wait expires
         if (c.bulk) {
           mbar_expect_tx(&full[s], (uint32_t)(c.n * GB));
           bulk_load(smem + s * STAGE, c.g, (uint32_t)(c.n * GB), &full[s]);
@@ -752,7 +776,7 @@ __global__ void __launch_bounds__(kSBThreads) k_grad_stats_bulk(StatsArgs a) {
           if (last_bulk[i] < 0) continue;
           const uint32_t parity = (last_bulk[i] / kSBStages) & 1;
           const uint64_t w0 = globaltimer();
-          while (!mbar_try_wait(&full[i], parity) && globaltimer() - w0 < kWaitLimitNs) {
+          while (!mbar_try_wait(&full[i], parity) && globaltimer() - w0 < a.fault.limit_ns) {
           }
         }
       }
@@ -769,7 +793,7 @@ __global__ void __launch_bounds__(kSBThreads) k_grad_stats_bulk(StatsArgs a) {
       const StatsChunk c = stats_chunk<GDT>(a, cur, seg, t, t1);
       t += c.tiles;
       const int s = k % kSBStages;
-      if (!mbar_wait(&full[s], (k / kSBStages) & 1, abort_flag)) break;
+      if (!mbar_wait(&full[s], (k / kSBStages) & 1, abort_flag, a.fault.limit_ns)) break;
       if (c.bulk) {
         const uint4* words = reinterpret_cast<const uint4*>(smem + s * STAGE);
         const int nw = (int)(c.n * GB / 16);
@@ -790,8 +814,9 @@ __global__ void __launch_bounds__(kSBThreads) k_grad_stats_bulk(StatsArgs a) {
     }
   }
   __syncthreads();
-  if (*abort_flag) acc = nan("");  // refuse the step: the partial counts as nonfinite
-  stats_tail(a, acc);
+  // a CTA that gave up refuses the step: its partial reports a time-out (see kTimeoutMark)
+  const bool aborted = *abort_flag != 0;
+  stats_tail(a, aborted ? 0.0 : acc, aborted);
 }
 
 __global__ void __launch_bounds__(kThreads) k_step_finalize(mb_adamw_plan p, mb_finalize_opts f) {
@@ -1010,7 +1035,8 @@ MB_API int mb_grad_stats(const mb_adamw_plan* p, const mb_finalize_opts* fin, mb
   if (fin && (rc = check_fin(fin))) return rc;
   const bool unscale = fin ? (fin->flags & MB_FIN_LOSS_SCALE) != 0 : false;
   StatsFn fn = pick_stats(p->grad_dtype, unscale);
-  StatsArgs a;
+  StatsArgs a{};
+  take_fault(kFaultStats, &a.fault.unit, &a.fault.limit_ns);
   a.segs = p->segs;
   a.n_tiles = p->n_tiles;
   a.n_segs = p->n_segs;
@@ -1063,6 +1089,7 @@ MB_API int mb_adamw_apply_tiles(const mb_adamw_plan* p, int64_t tile_lo, int64_t
   a.n_tiles = tile_hi;
   a.n_segs = p->n_segs;
   if (use_bulk_apply() && bulk.fn && bulk_ready(reinterpret_cast<const void*>(bulk.fn), bulk.smem)) {
+    take_fault(kFaultApply, &a.fault.unit, &a.fault.limit_ns);
     // kBulkCtasPerSm CTAs per SM; max_ctas counts register-staged CTAs (3 per SM)
     int64_t grid = (int64_t)sm_count() * kBulkCtasPerSm;
     if (max_ctas > 0) grid = max_ctas * kBulkCtasPerSm / 3 > 0 ? max_ctas * kBulkCtasPerSm / 3 : 1;
@@ -1098,6 +1125,7 @@ MB_API int mb_adamw_apply_tiles_peers(const mb_adamw_plan* p, int64_t tile_lo, i
   a.n_segs = p->n_segs;
   a.n_peers = n_peers;
   for (int i = 0; i < n_peers; ++i) a.peer_delta[i] = peer_deltas[i];
+  take_fault(kFaultApply, &a.fault.unit, &a.fault.limit_ns);
   int64_t grid = (int64_t)sm_count() * kBulkCtasPerSm;
   if (max_ctas > 0) grid = max_ctas * kBulkCtasPerSm / 3 > 0 ? max_ctas * kBulkCtasPerSm / 3 : 1;
   if (grid > tile_hi - tile_lo) grid = tile_hi - tile_lo;

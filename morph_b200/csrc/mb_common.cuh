@@ -237,8 +237,15 @@ struct GemmCall {
   int64_t upd_m, upd_n, upd_cols;
   float upd_scale, upd_cwd, upd_neglr;
   int32_t* err;
+  const int32_t* skip;  // optional device flag: nonzero = the launch returns at once
 };
 int gemm16(const GemmCall& call, cudaStream_t stream);
+
+// Test-only fault injection (mb_debug_arm_fault): the next launch of the named
+// kernel in this process takes the armed plan; every other launch gets
+// {unit -1, the default wait bound}.
+enum { kFaultApply = 1, kFaultStats = 2, kFaultGemm = 4 };
+void take_fault(int kernel, int64_t* unit, uint64_t* limit_ns);
 
 // Host-side validation of a fused AdamW plan and of finalize options (MB_OK or
 // the status the entry points return).

@@ -87,6 +87,8 @@ struct Args {
   float* upd_w[kMaxBatch];
   void* upd_out[kMaxBatch];
   int32_t* err;
+  const int32_t* skip;  // optional device flag: nonzero = return at once (a refused optimizer step)
+  FaultPlan fault;  // test-only: a tile whose first k-block is withheld, and the launch's wait bound
 };
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
@@ -255,6 +257,7 @@ __device__ __forceinline__ void store_chunk(const Args& g, float (&v)[32], int m
 template <bool kF16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args g) {
+  if (g.skip != nullptr && *g.skip != 0) return;  // before any barrier or TMEM allocation
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -263,7 +266,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;   // [2]: MMA -> epilogue
   uint64_t* acc_empty = acc_full + 2;    // [2]: epilogue -> MMA (4 arrivals: one per epilogue warp)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* drain = acc_empty + 2;       // on abort: completion of every MMA issued
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -278,6 +282,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 4);
     }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -302,7 +307,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb = 0; kb < KB; ++kb, ++kit) {
           const int s = kit % STAGES;
           const uint32_t round = kit / STAGES;
-          if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag)) break;
+          if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, g.fault.limit_ns)) break;
+          if (t == g.fault.unit && kb == 0) continue;  // test-only: withhold; the MMA warp's wait expires
           mbar_expect_tx(&full[s], A_STAGE + B_STAGE);
           tma_load_3d(sA + s * A_STAGE, &tmA, &full[s], kb * BK, bm * BM, mat);
           tma_load_3d(sB + s * B_STAGE, &tmB, &full[s], kb * BK, bn * BN, mat);
@@ -314,7 +320,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int k = kit - STAGES > 0 ? kit - STAGES : 0; k < kit; ++k) {
           const int s = k % STAGES;
           const uint32_t round = k / STAGES;
-          while (!mbar_try_wait(&full[s], round & 1) && globaltimer() - t0 < kWaitLimitNs) {
+          while (!mbar_try_wait(&full[s], round & 1) && globaltimer() - t0 < g.fault.limit_ns) {
           }
         }
       }
@@ -326,13 +332,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++it) {
         const int a = it & 1;
         const uint32_t use = it >> 1;
-        if (!mbar_wait(&acc_empty[a], (use & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(&acc_empty[a], (use & 1) ^ 1, abort_flag, g.fault.limit_ns)) break;
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(a * BN);
         for (int kb = 0; kb < KB; ++kb, ++kit) {
           const int s = kit % STAGES;
           const uint32_t round = kit / STAGES;
-          if (!mbar_wait(&full[s], round & 1, abort_flag)) break;
+          if (!mbar_wait(&full[s], round & 1, abort_flag, g.fault.limit_ns)) break;
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + s * A_STAGE), b0 = smem_u32(sB + s * B_STAGE);
 #pragma unroll
@@ -341,6 +347,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           umma_commit(&empty[s]);
         }
         umma_commit(&acc_full[a]);
+      }
+      if (*abort_flag) {
+        // every MMA this thread issued completes (bounded) before the accumulators are freed
+        umma_commit(drain);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < g.fault.limit_ns) {
+        }
       }
     }
   } else {
@@ -351,7 +364,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int a = it & 1;
       const uint32_t use = it >> 1;
       int ok = 0;
-      if (lane == 0) ok = mbar_wait(&acc_full[a], use & 1, abort_flag) && !*abort_flag;
+      if (lane == 0) ok = mbar_wait(&acc_full[a], use & 1, abort_flag, g.fault.limit_ns) && !*abort_flag;
       ok = __shfl_sync(0xffffffffu, ok, 0);  // warp-uniform: tcgen05.ld is .sync.aligned
       if (!ok) break;
       tc_fence_after();
@@ -496,6 +509,8 @@ int gemm16(const GemmCall& q, cudaStream_t stream) {
     }
   }
   g.err = q.err;
+  g.skip = q.skip;
+  take_fault(kFaultGemm, &g.fault.unit, &g.fault.limit_ns);
   static int sms = 0;
   if (sms == 0) {
     int dev = 0;

@@ -77,6 +77,7 @@ struct MuonSrc {
 struct MuonParams {
   float beta_lerp;  // .05
   float nesterov;   // .95
+  const int32_t* skip = nullptr;  // device flag: nonzero = the step changes nothing
 };
 
 // Nesterov input of one element (also writes the updated momentum when `write`).
@@ -118,6 +119,7 @@ __device__ __forceinline__ void muon_u4(float* mom, const void* src, const MuonP
 template <int GDT>
 __global__ void __launch_bounds__(kThreads) k_muon_sumsq(MuonSrc t, MuonParams p, int64_t total, bool vec,
                                                           double* partials, unsigned int* tickets, float* divisors) {
+  if (p.skip != nullptr && *p.skip != 0) return;  // a refused step: momentum untouched
   const int b = blockIdx.y;
   float* mom = t.mom[b];
   const void* src = t.src[b];
@@ -204,6 +206,7 @@ template <int GDT, int OUT>
 __global__ void __launch_bounds__(256) k_ns_normalize(MuonSrc t, MuonParams p, int64_t rows, int64_t cols,
                                                       int64_t ld_d, int64_t ld_t, size_t stride, const float* divisors,
                                                       float prescale, void* Dv, void* Tv, bool vec) {
+  if (p.skip != nullptr && *p.skip != 0) return;
   using T = typename Elem<OUT>::T;
   const int b = blockIdx.z;
   T* D = static_cast<T*>(Dv) + stride * b;
@@ -368,6 +371,7 @@ int ns_core(const MuonSrc& t, const MuonParams& p, int gdt, int batch, int64_t r
     g1.d = A; g1.ldd = mp; g1.sd = sa;
     g1.dt = A; g1.lddt = mp; g1.sdt = sa;
     g1.err = err;
+    g1.skip = p.skip;
     if ((rc = gemm16(g1, s))) return rc;
     // M = a I + b A + c A A, formed in FP32 and rounded once: the reference's
     // a X + (b A + c A A) X would add two nearly cancelling products.
@@ -381,6 +385,7 @@ int ns_core(const MuonSrc& t, const MuonParams& p, int gdt, int batch, int64_t r
     g2.d = B; g2.ldd = mp; g2.sd = sa;
     g2.dt = B; g2.lddt = mp; g2.sdt = sa;
     g2.err = err;
+    g2.skip = p.skip;
     if ((rc = gemm16(g2, s))) return rc;
     // X' = M X: X^T is the K-major operand. X' overwrites X (no longer read);
     // X'^T goes to the other XT buffer. The last iteration applies the update
@@ -392,6 +397,7 @@ int ns_core(const MuonSrc& t, const MuonParams& p, int gdt, int batch, int64_t r
     g3.M = mp; g3.N = np; g3.K = mp;
     g3.alpha = s1;
     g3.err = err;
+    g3.skip = p.skip;
     if (!last) {
       g3.d = X; g3.ldd = np; g3.sd = sx;
       g3.dt = XTn; g3.lddt = mp; g3.sdt = sx;
@@ -475,7 +481,7 @@ MB_API int mb_muon_step_batched(float* const* w, float* const* momentum, const v
   Layout L = layout_for(batch, rows, cols, false);
   if (workspace_bytes < L.total) return MB_ERR_ARG;
   if (!aligned(workspace, 256)) return MB_ERR_ALIGN;
-  MuonParams p{args->beta_lerp, args->nesterov};
+  MuonParams p{args->beta_lerp, args->nesterov, args->skip};
   const float coeffs[3] = {args->ns_a, args->ns_b, args->ns_c};
   Update upd{w, out_dtype == MB_NONE ? nullptr : out, out_dtype, args->shape_scale, args->cwd, args->neg_lr};
   return ns_core(t, p, grad_dtype, batch, rows, cols, args->ns_steps, coeffs, args->ns_dtype, &upd,

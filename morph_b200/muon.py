@@ -136,12 +136,14 @@ def batch_plan(count, rows, cols, workspace_limit):
     return [min(size, count - b) for b in range(0, count, size)]
 
 
-def muon_step_batched(params, moms, grads, outs, lr, weight_decay, ns_dtype="auto", err=None):
+def muon_step_batched(params, moms, grads, outs, lr, weight_decay, ns_dtype="auto", err=None, skip=None):
     """optimizer.py:52-61 for each of ``params`` (same-shape contiguous FP32 CUDA
     matrices on one device) in one kernel-4 call: momentum (FP32, in place),
     Nesterov blend, Newton-Schulz, shape scale, decoupled weight decay; ``outs``
     (optional, one 16-bit tensor each) receive the updated weights. ``err``
-    (int32 device flag) is raised when a bounded wait expires."""
+    (int32 device flag) is raised when a bounded wait expires. ``skip`` (device
+    address of an int32 flag, e.g. a finalized gate's skip) makes every launch
+    of the step return at once when the flag is set: nothing changes."""
     batch = len(params)
     if batch == 0:
         return
@@ -168,7 +170,7 @@ def muon_step_batched(params, moms, grads, outs, lr, weight_decay, ns_dtype="aut
     f = lambda x: float(np.float32(x))  # noqa: E731
     args = _lib.MuonArgs(f(.05), f(.95), f(NS_COEFFS[0]), f(NS_COEFFS[1]), f(NS_COEFFS[2]), 5,
                          f(max(1, rows / cols) ** .5), f(1 - lr * weight_decay), f(-lr),
-                         ns_operand_dtype(rows, cols, ns_dtype))
+                         ns_operand_dtype(rows, cols, ns_dtype), skip)
     odt = _lib.MB_NONE if outs is None else _lib.dtype_code(outs[0].dtype)
     table = ctypes.c_void_p * batch
     with torch.cuda.device(dev):
@@ -195,14 +197,18 @@ class HybridMuonAdamW:
     """Drop-in for streamtrain/optimizer.py:34-70 on the B200 kernels.
 
     Same constructor, attributes (muon, adam, momentum, lr, weight_decay),
-    zero_grad, step and state_dict/load_state_dict format. ``step`` first checks
-    every gradient for finiteness on the device (kernel 2 with the gate) and
-    raises FloatingPointError without touching any state if one is not finite;
-    then each Muon matrix takes one fused Muon step (kernel 4) and the AdamW
-    group one fused AdamW step (kernels 2 + 1)."""
+    zero_grad, step and state_dict/load_state_dict format. ``step`` enqueues
+    one device-side finiteness gate over every gradient (kernel 2 and its
+    finalize, optimizer.py:50-51), then each shape's Muon matrices (kernel 4,
+    batched) and the AdamW group (finalize and kernel 1); every launch reads the
+    gate's skip flag first, so a nonfinite gradient changes nothing anywhere.
+    The host reads the outcome once, at the end: with ``sync=True`` (the
+    default, the reference's behaviour) ``step`` raises FloatingPointError when
+    the gate refused the step; with ``sync=False`` it only enqueues and
+    ``check()`` raises later."""
 
     def __init__(self, model, lr=1e-3, muon_lr=None, weight_decay=.01, low_precision=None, ns_dtype="auto",
-                 workspace_limit=4 << 30):
+                 workspace_limit=4 << 30, sync=True):
         from .optim import AdamW
         self.muon, adam = partition(model)
         self.lr = lr if muon_lr is None else muon_lr
@@ -212,51 +218,87 @@ class HybridMuonAdamW:
         self.low_precision_copies = {}
         self.ns_dtype = ns_dtype
         self.workspace_limit = int(workspace_limit)
+        self.sync = bool(sync)
+        # the AdamW group finalizes from the gate's record over all gradients (gate on, no host read)
         self.adam = AdamW(adam, lr=lr, weight_decay=weight_decay, betas=(.9, .95), foreach=False,
-                          low_precision=low_precision)
+                          low_precision=low_precision, gate=True, sync=False)
+        self.adam._shared_record = True
         self._gate_engines = {}
         self._err = {}
+        self._new_momentum = []
 
     def zero_grad(self, set_to_none=True):
         for p in self.muon:
             p.grad = None if set_to_none else torch.zeros_like(p)
         self.adam.zero_grad(set_to_none=set_to_none)
 
-    def _check_finite(self, params):
-        """Device finiteness gate over every gradient (optimizer.py:50-51)."""
+    def _record_engine(self, device):
+        """The step engine whose device record the gate writes and every launch
+        of the step reads: the AdamW group's (it finalizes from it)."""
+        adam_params = [p for g in self.adam.param_groups for p in g["params"]]
+        if adam_params:
+            return self.adam._engine_for(adam_params[0].device)
+        from .optim import StepEngine
+        eng = self._gate_engines.get(("record", device))
+        if eng is None:
+            eng = self._gate_engines[("record", device)] = StepEngine(device)
+        return eng
+
+    def _gate(self, params):
+        """Enqueue kernel 2 over every gradient into the shared record and finalize
+        it with the finiteness gate (optimizer.py:50-51). Returns the record's
+        engine, or None when no parameter has a gradient."""
         from .optim import StepEngine
         grads = [(p, p.grad) for p in params if p.grad is not None]
         if not grads:
-            return
+            return None
+        dev = grads[0][1].device
+        rec_eng = self._record_engine(dev)
         by_dtype = {}
         for p, g in grads:
+            if g.device != dev:
+                raise ValueError("all gradients of one HybridMuonAdamW must live on one CUDA device")
             by_dtype.setdefault(g.dtype, []).append((p, g.contiguous()))
+        fin = None
+        plans = []
         for dtype, items in by_dtype.items():
-            dev = items[0][1].device
             eng = self._gate_engines.get((dev, dtype))
             if eng is None:
                 eng = self._gate_engines[(dev, dtype)] = StepEngine(dev)
+            eng.state_buf = rec_eng.state_buf
             for p, _ in items:
                 eng.slot(p, 0)
             entries = [(g, g, g, g, None, 0) for _, g in items]
             plan = eng.prepare(entries, [(0.0, 0.9, 0.9, 1e-8, 0.0, "torch")], _lib.dtype_code(dtype), _lib.MB_NONE,
                                keys=[p for p, _ in items])
             fin = eng.finalize_opts(_lib.MB_FIN_GATE, None)
-            with torch.cuda.device(dev):
-                _lib.check(eng.lib.mb_grad_stats(ctypes.byref(plan), ctypes.byref(fin), _lib.stream_handle()))
-            if eng.read_state().status:
-                raise FloatingPointError('nonfinite gradient; optimizer not updated')
+            plans.append((eng, plan))
+        record = rec_eng.state_buf[:16].view(torch.float64)
+        with torch.cuda.device(dev):
+            s = _lib.stream_handle()
+            if len(plans) == 1:
+                eng, plan = plans[0]
+                _lib.check(eng.lib.mb_grad_stats(ctypes.byref(plan), ctypes.byref(fin), s))
+            else:  # one record over several gradient dtypes, then one finalize
+                acc = torch.zeros(2, dtype=torch.float64, device=dev)
+                for eng, plan in plans:
+                    _lib.check(eng.lib.mb_grad_stats(ctypes.byref(plan), None, s))
+                    acc += record
+                record.copy_(acc)
+                eng, plan = plans[-1]
+                _lib.check(eng.lib.mb_step_finalize(ctypes.byref(plan), ctypes.byref(fin), s))
+        return rec_eng
 
     @torch.no_grad()
     def step(self):
         all_params = self.muon + [p for g in self.adam.param_groups for p in g['params']]
-        self._check_finite(all_params)
-        for dev, err in self._err.items():  # the gate above synchronised: last step's flags are final
-            if int(err.item()):
-                err.zero_()
-                raise RuntimeError("muon step: a bounded wait expired on the device")
+        rec_eng = self._gate(all_params)
+        if rec_eng is None:
+            return
+        skip = rec_eng.state_buf.data_ptr() + _lib.StepState.skip.offset
         # matrices of one shape and gradient dtype share every launch (kernel 4 batches them)
         groups = {}
+        self._new_momentum = []
         for i, p in enumerate(self.muon):
             if p.grad is None:
                 continue
@@ -264,16 +306,42 @@ class HybridMuonAdamW:
                 raise ValueError("Muon parameters must be contiguous 2-D float32 CUDA tensors")
             if i not in self.momentum:
                 self.momentum[i] = torch.zeros_like(p)
+                self._new_momentum.append(i)
             g = p.grad.contiguous()
             groups.setdefault((p.device, tuple(p.shape), g.dtype), []).append((p, self.momentum[i], g))
         for (dev, (rows, cols), _), items in groups.items():
             b = 0
             for size in batch_plan(len(items), rows, cols, self.workspace_limit):
-                self._muon_batch(items[b:b + size], rows, cols)
+                self._muon_batch(items[b:b + size], rows, cols, skip)
                 b += size
         self.adam.step()
+        if self.sync:
+            self.check()
 
-    def _muon_batch(self, items, rows, cols):
+    def check(self):
+        """Wait for the last step and raise what it reported: FloatingPointError
+        if the gate refused it (nothing changed; momentum buffers it created are
+        dropped, as the reference never creates them), RuntimeError if a
+        bounded device wait expired."""
+        for dev, err in self._err.items():
+            if int(err.item()):
+                err.zero_()
+                raise RuntimeError("muon step: a bounded wait expired on the device")
+        adam_params = [p for g in self.adam.param_groups for p in g["params"]]
+        dev = adam_params[0].device if adam_params else (self.muon[0].device if self.muon else None)
+        if dev is None:
+            return
+        st = self._record_engine(dev).read_state()
+        if st.status:
+            for i in self._new_momentum:
+                self.momentum.pop(i, None)
+            self._new_momentum = []
+            if int(st.status) == _lib.MB_ERR_NONFINITE:
+                raise FloatingPointError('nonfinite gradient; optimizer not updated')
+            _lib.check(int(st.status), "optimizer not updated")
+        self._new_momentum = []
+
+    def _muon_batch(self, items, rows, cols, skip=None):
         """One kernel-4 step over matrices of one shape (optimizer.py:52-61 per matrix)."""
         dev = items[0][0].device
         outs = None
@@ -288,7 +356,7 @@ class HybridMuonAdamW:
         if err is None:
             err = self._err[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
         muon_step_batched([p for p, _, _ in items], [m for _, m, _ in items], [g for _, _, g in items], outs,
-                          self.lr, self.weight_decay, self.ns_dtype, err)
+                          self.lr, self.weight_decay, self.ns_dtype, err, skip)
 
     def state_dict(self):
         return dict(momentum=self.momentum, adam=self.adam.state_dict(), lr=self.lr, weight_decay=self.weight_decay)

@@ -234,10 +234,14 @@ class StepEngine:
             _lib.check(self.lib.mb_step_finalize(ctypes.byref(plan), ctypes.byref(fin), s), "mb_step_finalize")
         _lib.check(self.lib.mb_adamw_apply(ctypes.byref(plan), s), "mb_adamw_apply")
 
-    def step(self, entries, groups, grad_dtype, out_dtype, fin_flags, max_norm, stream=None):
+    def step(self, entries, groups, grad_dtype, out_dtype, fin_flags, max_norm, stream=None, stats=None):
+        """One step; ``stats=False`` skips kernel 2 and finalizes from the
+        {sum of squares, nonfinite} record already in the state (written by an
+        earlier statistics launch over a superset of the gradients)."""
         plan = self.prepare(entries, groups, grad_dtype, out_dtype)
-        stats = bool(fin_flags & (_lib.MB_FIN_LOSS_SCALE | _lib.MB_FIN_GATE | _lib.MB_FIN_CLIP_TORCH
-                                  | _lib.MB_FIN_CLIP_DISK))
+        if stats is None:
+            stats = bool(fin_flags & (_lib.MB_FIN_LOSS_SCALE | _lib.MB_FIN_GATE | _lib.MB_FIN_CLIP_TORCH
+                                      | _lib.MB_FIN_CLIP_DISK))
         self.launch(plan, self.finalize_opts(fin_flags, max_norm), stream, stats)
         return plan
 
@@ -281,6 +285,9 @@ class AdamW(torch.optim.Optimizer):
         self.low_precision_copies: dict[torch.Tensor, torch.Tensor] = {}
         self._engine: StepEngine | None = None
         self._generation = 0
+        # set by HybridMuonAdamW: the statistics of this step were computed over
+        # all of the hybrid's gradients into this engine's record already
+        self._shared_record = False
         # per parameter, after its first step: (p, its state dict, copy, device, shape)
         self._prepared: dict[int, tuple] = {}
 
@@ -370,7 +377,8 @@ class AdamW(torch.optim.Optimizer):
             self._prepared.clear()
         odt = _lib.dtype_code(self.low_precision) if self.low_precision is not None else _lib.MB_NONE
         with torch.cuda.device(device):
-            eng.step(entries, groups, gdt, odt, self._fin_flags(), self.max_norm)
+            eng.step(entries, groups, gdt, odt, self._fin_flags(), self.max_norm,
+                     stats=False if self._shared_record else None)
         if self.sync:
             self.check()
         return loss

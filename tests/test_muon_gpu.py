@@ -309,3 +309,74 @@ def test_adam_group_matches_torch_adamw_bit_exactly(cuda):
         hybrid.step()
     for key, value in model.state_dict().items():
         torch.testing.assert_close(value, before[key], rtol=0, atol=0)
+
+
+def _hybrid_model(cuda, seed):
+    torch.manual_seed(seed)
+    model = torch.nn.Sequential(torch.nn.Linear(256, 512, bias=False), torch.nn.Linear(512, 256, bias=False),
+                                torch.nn.LayerNorm(256)).to(cuda)
+    gen = torch.Generator(device=cuda).manual_seed(seed + 1)
+    for p in model.parameters():
+        p.grad = torch.randn(p.shape, device=cuda, generator=gen) * 1e-3
+    return model
+
+
+def test_hybrid_gate_is_read_once_and_sync_false_defers_it(cuda):
+    """The finiteness gate runs on the device; every launch of the step reads its
+    skip flag. sync=False: step() raises nothing, check() raises FloatingPointError
+    afterwards, and no parameter, momentum or AdamW state changed."""
+    from morph_b200 import HybridMuonAdamW
+    model = _hybrid_model(cuda, 5)
+    opt = HybridMuonAdamW(model, lr=.02, sync=False)
+    opt.step()
+    opt.check()
+    before = {k: v.clone() for k, v in model.state_dict().items()}
+    mom = {i: m.clone() for i, m in opt.momentum.items()}
+    adam_state = {id(p): (st["exp_avg"].clone(), st["exp_avg_sq"].clone(), int(st["step"]))
+                  for p, st in opt.adam.state.items()}
+    model[2].bias.grad[3] = float("nan")  # an AdamW-group gradient
+    opt.step()  # enqueues only
+    with pytest.raises(FloatingPointError):
+        opt.check()
+    for k, v in model.state_dict().items():
+        assert torch.equal(v, before[k]), k
+    for i, m in opt.momentum.items():
+        assert torch.equal(m, mom[i])
+    for p, st in opt.adam.state.items():
+        a, b, t = adam_state[id(p)]
+        assert torch.equal(st["exp_avg"], a) and torch.equal(st["exp_avg_sq"], b) and int(st["step"]) == t
+    # a Muon gradient: the default sync=True raises from step() itself
+    opt2 = HybridMuonAdamW(_hybrid_model(cuda, 6), lr=.02)
+    opt2.muon[0].grad[0, 0] = float("inf")
+    with pytest.raises(FloatingPointError):
+        opt2.step()
+    assert opt2.momentum == {}  # as the reference, which raises before creating any
+
+
+def test_hybrid_step_replays_from_a_cuda_graph(cuda):
+    """With sync=False the whole hybrid step (gate, batched Muon, AdamW) is a
+    pure kernel sequence: captured after one eager step, its replays equal eager
+    steps bit for bit."""
+    from morph_b200 import HybridMuonAdamW
+    ma, mb = _hybrid_model(cuda, 7), _hybrid_model(cuda, 7)
+    oa = HybridMuonAdamW(ma, lr=.02, sync=False)
+    ob = HybridMuonAdamW(mb, lr=.02, sync=False)
+    for _ in range(4):
+        oa.step()
+    ob.step()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(cuda)
+    side.wait_stream(torch.cuda.current_stream(cuda))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+        ob.step()
+    torch.cuda.current_stream(cuda).wait_stream(side)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    oa.check()
+    ob.check()
+    for (k, a), b in zip(ma.state_dict().items(), mb.state_dict().values()):
+        assert torch.equal(a, b), k
+    for i in oa.momentum:
+        assert torch.equal(oa.momentum[i], ob.momentum[i])
