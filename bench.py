@@ -384,8 +384,7 @@ def run_morph(args, rank, world, local_rank):
                                 "kind": "reference",
                                 "sample": f"1 of 42 layers ({n:,} params), clip_grad_norm_ + "
                                           "torch.optim.AdamW(foreach=False), 3 timed steps"}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return line
 
 
 def ns_flops(rows, cols, steps=5):
@@ -465,7 +464,7 @@ def config4_workload(args):
     return f"config4 reduced for profiling: {args.c4_layers} layers"
 
 
-def run_config4_zero(args, rank, world, local_rank):
+def run_config4_zero(args, rank, world, local_rank, emit=True):
     """Config 4 on N GPUs: ZeroHybridMuonAdamW (whole Muon matrices dealt over
     the ranks, AdamW group flat-sharded, BF16 weights all-gathered per round).
     Time per step = max over ranks of the device-timed step."""
@@ -513,10 +512,13 @@ def run_config4_zero(args, rank, world, local_rank):
                              "unit": "TFLOP/s", "frac": achieved / (peak * world),
                              "basis": "whole step time, algorithmic NS FLOPs"},
                 "clocks": clk.summary()}
-        print(json.dumps(line), flush=True)
+        if emit:
+            print(json.dumps(line), flush=True)
+        return line
+    return None
 
 
-def run_config4(args):
+def run_config4(args, emit=True):
     """Config 4: hybrid Muon + AdamW at the 7B shape, one GPU. Muon: 32 layers x
     {3 x [4096, 11008], 4 x [4096, 4096]} FP32 masters and momentum, BF16 grads
     N(0, 1e-4), Newton-Schulz 5 iterations on BF16 tcgen05 GEMMs. AdamW: a
@@ -529,7 +531,8 @@ def run_config4(args):
     torch.cuda.set_device(device)
 
     model = config4_model(device, args.c4_layers)
-    opt = HybridMuonAdamW(model, lr=3e-4, weight_decay=.1, ns_dtype="bf16")
+    # sync=False: step() only enqueues (the gate is read on the device); checked after the timed region
+    opt = HybridMuonAdamW(model, lr=3e-4, weight_decay=.1, ns_dtype="bf16", sync=False)
     muon_params = sum(p.numel() for p in opt.muon)
     adam_params = sum(p.numel() for g in opt.adam.param_groups for p in g["params"])
     for _ in range(args.warmup):
@@ -542,6 +545,7 @@ def run_config4(args):
             opt.step()
         stop.record()
         torch.cuda.synchronize()
+    opt.check()  # every timed step was applied
     step_ms = start.elapsed_time(stop) / args.steps
     # Muon step of one matrix, and of the batch the optimizer launches for the
     # shape (momentum + normalise + 5 NS iterations + update), timed alone
@@ -617,7 +621,9 @@ def run_config4(args):
                                           "shape on the host cores, scaled by the shape counts; the AdamW group "
                                           "(4% of the parameters, <1% of the work) is not included",
                                 "per_matrix_s": sample}
-    print(json.dumps(line), flush=True)
+    if emit:
+        print(json.dumps(line), flush=True)
+    return line
 
 
 def host_link_gbs(device, nbytes=1 << 30):
@@ -848,7 +854,7 @@ def run_extra(args):
     print(json.dumps(out), flush=True)
 
 
-def run_config1(args):
+def run_config1(args, emit=True):
     """Config 1 (and the latency side of config 3): 64 x [128, 128] FP32 masters,
     FP16 grads x 2^16 with the device loss scale (2^16, growth 2000), lr 3e-4,
     betas (.9, .95), eps 1e-8, wd .1, FP16 copy of the weights every step.
@@ -923,10 +929,12 @@ def run_config1(args):
             "cpu_baseline": {"value": cpu_us, "unit": "us/step", "cores": threads, "kind": "reference",
                              "sample": "unscale + torch.optim.AdamW(foreach=False) + FP16 copy on the same shapes"},
             "gpu_launches_per_step": 2}
-    print(json.dumps(line), flush=True)
+    if emit:
+        print(json.dumps(line), flush=True)
+    return line
 
 
-def run_config5(args, rank=0, world=1, local_rank=0):
+def run_config5(args, rank=0, world=1, local_rank=0, emit=True):
     """Config 5: lazy row-sparse AdamW with the [262144, 3072] table's w, m, v in
     pinned host memory, 10% of rows (sorted unique int64) touched per step with
     FP16 grads N(0, 1e-3), DiskState.update hyperparameters (lr 1e-4, clip 1.0),
@@ -937,17 +945,18 @@ def run_config5(args, rank=0, world=1, local_rank=0):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     rows, cols, k = 262144, 3072, 26214
-    gen = torch.Generator().manual_seed(1234)
-    init = torch.empty(rows, cols)
-    init.normal_(0.0, 0.02, generator=gen)
     if world > 1:
         import torch.distributed as dist
-        table = ShardedRowTable(rows, cols, init=init, device=device)
-        window_rows = table.local.window_rows
+        table = ShardedRowTable(rows, cols, device=device)
+        local = table.local
     else:
-        table = OffloadedRowTable(rows, cols, init=init, device=device)
-        window_rows = table.window_rows
-    del init
+        table = local = OffloadedRowTable(rows, cols, device=device)
+    window_rows = local.window_rows
+    # masters N(0, 0.02), drawn on the device and copied into the pinned planes
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    for r0 in range(0, local.rows, 8192):
+        r1 = min(local.rows, r0 + 8192)
+        local.w[r0:r1].copy_(torch.empty(r1 - r0, cols, device=device).normal_(0.0, 0.02, generator=gen))
     steps = args.warmup + args.steps
     idxs, grads = [], []
     gdev = torch.Generator(device=device).manual_seed(99)
@@ -999,7 +1008,168 @@ def run_config5(args, rank=0, world=1, local_rank=0):
         line["cpu_baseline"] = {"value": k * cols / (sum(ref_times) / len(ref_times)), "unit": "touched params/s",
                                 "cores": threads, "kind": "reference",
                                 "sample": "disk.py:210-215 arithmetic on the gathered [26214, 3072] rows in RAM"}
-    print(json.dumps(line), flush=True)
+    if emit:
+        print(json.dumps(line), flush=True)
+    return line
+
+
+def zero_parity_check(opt, grads, shapes, sizes, rank, world, local_rank):
+    """Correctness of the sharded step inside the measured run (N > 1).
+
+    * replicas: per-chunk sums of the 32-bit words of every rank's full
+      low-precision weight buffer are all-gathered and must be identical;
+    * sampled pieces: the first and last ZeRO piece of each rank (the first one
+      of every rank but 0 starts mid-tensor), up to 1M elements each, are
+      snapshotted before one more fused step and recomputed on the same GPU as
+      a stand-alone one-GPU AdamW step (mb_step_finalize from the all-reduced
+      {sum of squares, nonfinite} record, then mb_adamw_apply); w, m, v, the
+      BF16 copy at the piece's place in the gathered weights and the clip
+      coefficient must be bit-identical. The one-GPU kernels are the ones the
+      GPU parity tests hold bit-exact to the CPU oracle."""
+    import ctypes
+    import torch.distributed as dist
+    from morph_b200 import _lib
+    from morph_b200.optim import StepEngine
+    device = opt.device
+    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64).tolist()
+    flat_g = [g.reshape(-1) for g in grads]
+    eng0 = opt.backend.engine
+    owned = [j for j, pc in enumerate(opt.pieces) if pc[3] > 0]
+    picks = []
+    for j in sorted({owned[0], owned[-1]}) if owned else []:
+        i, t_off, s_off, n, _ = opt.pieces[j]
+        n = min(n, 1 << 20)
+        picks.append(dict(i=i, t_off=t_off, s_off=s_off, n=n, w=opt.master[s_off:s_off + n].clone(),
+                          m=opt.exp_avg[s_off:s_off + n].clone(), v=opt.exp_avg_sq[s_off:s_off + n].clone(),
+                          g=flat_g[i][t_off:t_off + n].clone(),
+                          clock=int(eng0.clocks[eng0.slots[id(opt._keys[j])]])))
+    torch.cuda.synchronize(device)
+    opt.step(grads)
+    torch.cuda.synchronize(device)
+    info = opt.last_step()
+    ok = info["status"] == 0 and not info["skipped"]
+    record = opt.backend.record().clone()
+    lib = _lib.lib()
+    for pk in picks:
+        eng = StepEngine(device)
+        key = object()
+        eng.slot(key, pk["clock"])
+        out = torch.empty(pk["n"], dtype=opt.low_precision, device=device)
+        plan = eng.prepare([(pk["w"], pk["m"], pk["v"], pk["g"], out, 0)],
+                           [(opt.lr, opt.betas[0], opt.betas[1], opt.eps, opt.weight_decay, "torch")],
+                           _lib.dtype_code(pk["g"].dtype), _lib.dtype_code(opt.low_precision), keys=[key])
+        eng.state_buf[:16].copy_(record.view(torch.uint8))
+        fin = eng.finalize_opts(opt._fin_flags(), opt.max_norm)
+        with torch.cuda.device(device):
+            _lib.check(lib.mb_step_finalize(ctypes.byref(plan), ctypes.byref(fin), _lib.stream_handle()))
+            _lib.check(lib.mb_adamw_apply(ctypes.byref(plan), _lib.stream_handle()))
+        torch.cuda.synchronize(device)
+        s_off, n = pk["s_off"], pk["n"]
+        f_off = offsets[pk["i"]] + pk["t_off"]
+        ok = ok and torch.equal(pk["w"], opt.master[s_off:s_off + n])
+        ok = ok and torch.equal(pk["m"], opt.exp_avg[s_off:s_off + n])
+        ok = ok and torch.equal(pk["v"], opt.exp_avg_sq[s_off:s_off + n])
+        ok = ok and torch.equal(out.view(torch.int16), opt.flat_weights[f_off:f_off + n].view(torch.int16))
+        ok = ok and np.float32(eng.read_state().clip_coef) == np.float32(info["clip_coef"])
+    total = sum(sizes)
+    words = opt.flat_weights[:total - total % 2].view(torch.int32)
+    chunk = 1 << 22
+    sums = torch.stack([words[a:a + chunk].sum(dtype=torch.int64) for a in range(0, words.numel(), chunk)])
+    gathered = [torch.empty_like(sums) for _ in range(world)]
+    dist.all_gather(gathered, sums)
+    replicas = all(torch.equal(gathered[0], x) for x in gathered[1:])
+    flags = torch.tensor([int(ok), len(picks), sum(int(p["t_off"] > 0) for p in picks),
+                          sum(p["n"] for p in picks)], dtype=torch.int64, device=device)
+    low = flags.clone()
+    dist.all_reduce(low, op=dist.ReduceOp.MIN)
+    dist.all_reduce(flags)
+    return {"replicas_identical": bool(replicas), "sampled_bit_exact": bool(low[0]),
+            "pieces_checked": int(flags[1]), "pieces_starting_mid_tensor": int(flags[2]),
+            "elements_checked": int(flags[3]),
+            "method": "per-chunk word sums of every rank's gathered BF16 weights compared across ranks; the first "
+                      "and last ZeRO piece of each rank recomputed as a one-GPU AdamW step from the all-reduced "
+                      "norm record (w, m, v, BF16 copy in the gathered buffer, clip coefficient bit-identical)"}
+
+
+def run_update_only(args, rank, world, local_rank, shapes, sizes):
+    """The update alone at N > 1: each rank runs a complete AdamW step over its
+    own contiguous 1/N shard of config 2 (fresh FP32 w, m, v, BF16 gradients and
+    a BF16 copy of the shard) with the global norm all-reduced, and no
+    all-gather of the copies. Separate buffers from the sharded optimizer, so
+    its state is untouched. Time per step = max over ranks."""
+    import ctypes
+    import torch.distributed as dist
+    from morph_b200 import _lib
+    from morph_b200.optim import StepEngine
+    device = torch.device("cuda", local_rank)
+    total = sum(sizes)
+    lo, hi = shard_bounds(total, world, rank)
+    n_local = hi - lo
+    gen = torch.Generator(device=device).manual_seed(4321 + rank)
+    w = torch.empty(n_local, dtype=torch.float32, device=device)
+    g = torch.empty(n_local, dtype=torch.bfloat16, device=device)
+    for s0 in range(0, n_local, 1 << 28):
+        e0 = min(n_local, s0 + (1 << 28))
+        w[s0:e0].normal_(0.0, 0.02, generator=gen)
+        g[s0:e0] = torch.empty(e0 - s0, device=device).normal_(0.0, 1e-4, generator=gen).to(torch.bfloat16)
+    m, v = torch.zeros_like(w), torch.zeros_like(w)
+    out = torch.empty(n_local, dtype=torch.bfloat16, device=device)
+    eng = StepEngine(device)
+    entries, off = [], 0
+    for n in sizes:
+        a, b = max(off, lo), min(off + n, hi)
+        if a < b:
+            o = a - lo
+            eng.slot(w[o:o + b - a], 0)
+            entries.append((w[o:o + b - a], m[o:o + b - a], v[o:o + b - a], g[o:o + b - a], out[o:o + b - a], 0))
+        off += n
+    plan = eng.prepare(entries, [(LR, BETAS[0], BETAS[1], EPS, WD, "torch")], _lib.MB_BF16, _lib.MB_BF16)
+    fin = eng.finalize_opts(_lib.MB_FIN_CLIP_TORCH | _lib.MB_FIN_GATE, MAX_NORM)
+    pp, pf = ctypes.byref(plan), ctypes.byref(fin)
+    record = eng.state_buf[:16].view(torch.float64)
+    lib = eng.lib
+    steps = max(1, min(args.steps, 5))
+
+    def one_step(evs=None):
+        s = _lib.stream_handle()
+        _lib.check(lib.mb_grad_stats(pp, None, s))
+        dist.all_reduce(record)
+        _lib.check(lib.mb_step_finalize(pp, pf, s))
+        if evs is not None:
+            evs[0].record()
+        _lib.check(lib.mb_adamw_apply(pp, s))
+        if evs is not None:
+            evs[1].record()
+
+    for _ in range(3):
+        one_step()
+    dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        one_step(evs[i])
+    stop.record()
+    torch.cuda.synchronize()
+    st = eng.read_state()
+    t = torch.tensor([start.elapsed_time(stop) / steps, sum(e[0].elapsed_time(e[1]) for e in evs) / steps,
+                      float(st.status or st.skip)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, apply_ms, bad = t.tolist()
+    if bad:
+        raise RuntimeError("update-only step refused")
+    hbm, peak_kind = measured_peaks()
+    owned = torch.tensor([n_local], dtype=torch.int64, device=device)
+    dist.all_reduce(owned, op=dist.ReduceOp.MAX)
+    achieved = APPLY_BYTES * int(owned) / (apply_ms / 1e3) / 1e9
+    return {"value": total / (ms / 1e3), "unit": "params/s", "ms_per_step": ms, "steps": steps,
+            "kernels_ms": {"adamw_apply": apply_ms},
+            "roofline": {"bound": "hbm", "kernel": "mb_adamw_apply", "achieved": achieved, "peak": hbm,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
+                         "algorithmic_bytes_per_launch": APPLY_BYTES * int(owned)},
+            "workload": f"each rank's contiguous 1/{world} of config 2: kernel 2, all-reduce of the norm record, "
+                        "finalize, kernel 1 with the BF16 copy of the shard; no all-gather"}
 
 
 def run_morph_zero(args, rank, world, local_rank):
@@ -1139,7 +1309,9 @@ def run_morph_zero(args, rank, world, local_rank):
     if opt.peer_writes:
         # fused update + all-gather: the slower of the HBM work and the NVLink sends bounds the launch
         link_bytes = 2 * owned * (world - 1)
-        t_hbm = APPLY_BYTES * owned / (hbm * 1e9)
+        # this rank's own 28 B/param plus the other ranks' BF16 copies landing in its HBM
+        hbm_bytes = APPLY_BYTES * owned + 2 * (total - owned)
+        t_hbm = hbm_bytes / (hbm * 1e9)
         t_link = link_bytes / (NVLINK_GBS * 1e9)
         roofline = {"bound": "nvlink" if t_link > t_hbm else "hbm", "kernel": "mb_adamw_apply_tiles_peers",
                     "achieved": (max(t_hbm, t_link) / (apply_ms / 1e3)), "peak": 1.0, "unit": "of target time",
@@ -1147,13 +1319,14 @@ def run_morph_zero(args, rank, world, local_rank):
                     "target_ms": 1e3 * max(t_hbm, t_link), "hbm_ms": 1e3 * t_hbm, "nvlink_ms": 1e3 * t_link,
                     "nvlink_bytes_per_rank": link_bytes, "nvlink_peak_gbs": NVLINK_GBS,
                     "nvlink_achieved_gbs": link_bytes / (apply_ms / 1e3) / 1e9,
-                    "hbm_achieved_gbs": achieved, "hbm_peak": hbm, "peak_kind": peak_kind,
+                    "hbm_achieved_gbs": hbm_bytes / (apply_ms / 1e3) / 1e9, "hbm_bytes_per_rank": hbm_bytes,
+                    "hbm_peak": hbm, "peak_kind": peak_kind,
                     "algorithmic_bytes_per_launch": APPLY_BYTES * owned,
                     "traffic": APPLY_TRAFFIC_PER_PARAM * owned,
                     "traffic_basis": "ncu one-layer capture scaled by params per launch (HBM side)",
                     "note": "kernel 1 stores each BF16 copy into every rank's buffer over NVLink (peer "
-                            "pointers); target = max(HBM bytes / measured HBM peak, NVLink bytes / "
-                            "measured 770 GB/s peer copy)"}
+                            "pointers); target = max(HBM bytes (own 28 B/param + 2 B/param received from "
+                            "the other ranks) / measured HBM peak, NVLink bytes / measured 770 GB/s peer copy)"}
     line = {
         "metric": METRIC, "value": total / (ms_per_step / 1e3), "unit": "params/s", "n_gpus": world,
         "steps": k, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -1174,9 +1347,9 @@ def run_morph_zero(args, rank, world, local_rank):
     }
     if e2e is not None:
         line["e2e"] = e2e
+    line["parity"] = zero_parity_check(opt, grads, shapes, sizes, rank, world, local_rank)
     opt.close()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return line
 
 
 def run_e2e(args, device, shapes, sizes, w, m, v, g, out):
@@ -1254,6 +1427,53 @@ def run_e2e(args, device, shapes, sizes, w, m, v, g, out):
                     "overlaps step k's update (two device gradient buffers)"}
 
 
+def _summary(line):
+    """The fields of a config's own line kept in the headline line's ``configs``."""
+    keep = ("metric", "value", "unit", "ms_per_step", "higher_is_better", "n_gpus", "steps", "warmup", "dtype",
+            "roofline", "clocks", "cpu_baseline", "eager_us_per_step", "eager_device_us_per_step",
+            "graph_replay_us_per_step", "per_matrix")
+    out = {k: line[k] for k in keep if k in line}
+    out["workload"] = line.get("config", {}).get("workload")
+    out["parallelism"] = line.get("config", {}).get("parallelism")
+    return out
+
+
+def run_sub_configs(args, rank, world, local_rank):
+    """BASELINE configs 1, 4 and 5 measured in the same run as the headline
+    (one GPU), and configs 4 and 5 sharded at N > 1 (config 1 is a single-GPU
+    latency case). Each keeps its own metric, roofline and clock record."""
+    import gc
+    sub = argparse.Namespace(**vars(args))
+    sub.warmup = 3
+    out = {}
+
+    def fresh():
+        gc.collect()
+        torch.cuda.empty_cache()
+
+    fresh()
+    if world == 1:
+        out["config1"] = _summary(run_config1(sub, emit=False))
+        fresh()
+        sub.steps = min(args.steps, 5)
+        out["config4"] = _summary(run_config4(sub, emit=False))
+        fresh()
+        sub.steps = min(args.steps, 10)
+        out["config5"] = _summary(run_config5(sub, emit=False))
+    else:
+        sub.steps = min(args.steps, 5)
+        line = run_config4_zero(sub, rank, world, local_rank, emit=False)
+        if line is not None:
+            out["config4"] = _summary(line)
+        fresh()
+        sub.steps = min(args.steps, 10)
+        line = run_config5(sub, rank, world, local_rank, emit=False)
+        if line is not None:
+            out["config5"] = _summary(line)
+    fresh()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -1274,6 +1494,8 @@ def main():
     ap.add_argument("--c4-layers", type=int, default=32, help="profiling only: fewer layers than config 4")
     ap.add_argument("--ns-shape", default=None, help="profiling only, with --config 4: one matrix, e.g. 4096x4096")
     ap.add_argument("--rows", type=int, default=262144, help="--extra rows: table rows (profiling: fewer)")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="config 2 only: skip the configs 1/4/5 records measured after the headline")
     ap.add_argument("--extra", choices=["disk", "rows", "accum", "export", "all"], default=None,
                     help="measure a path beside the configs' step instead (one GPU)")
     args = ap.parse_args()
@@ -1308,10 +1530,20 @@ def main():
             run_config4_zero(args, rank, world, local_rank)
         elif world > 1 and args.config == 5:
             run_config5(args, rank, world, local_rank)
-        elif world > 1:
-            run_morph_zero(args, rank, world, local_rank)
         else:
-            run_morph(args, rank, world, local_rank)
+            full = args.layers == 42 and not args.no_embedding
+            if world > 1:
+                line = run_morph_zero(args, rank, world, local_rank)
+                torch.cuda.empty_cache()
+                shapes = config2_shapes(args.layers, not args.no_embedding)
+                line["update_only"] = run_update_only(args, rank, world, local_rank, shapes,
+                                                      [numel(s) for _, s in shapes])
+            else:
+                line = run_morph(args, rank, world, local_rank)
+            if full and not args.no_configs:
+                line["configs"] = run_sub_configs(args, rank, world, local_rank)
+            if rank == 0:
+                print(json.dumps(line), flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist
