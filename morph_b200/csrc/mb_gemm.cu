@@ -50,7 +50,13 @@ constexpr int kGemmThreads = kWarps * 32;
 constexpr int A_STAGE = BM * BK * 2;   // 16 KiB
 constexpr int B_STAGE = BN * BK * 2;   // 32 KiB
 constexpr int kBarrierBytes = 256;  // full/empty rings, 2 x acc full/empty, TMEM slot, abort flag
-constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + 1024 + kBarrierBytes;
+// Epilogue staging: each epilogue warp owns 32 rows of 64 B (a 32 x 32 16-bit
+// block) padded to 80 B, so a lane's own 16-byte row accesses are bank-conflict
+// free while the warp's global accesses go out as 8 rows x 64 B per instruction.
+constexpr int kStageRow = 80;
+constexpr int kStageRowF = 144;  // the fused update's FP32 rows: 128 B + 16 B pad
+constexpr int kStageWarp = 32 * kStageRowF;
+constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + 1024 + kBarrierBytes + 4 * kStageWarp;
 constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
 
 // Instruction descriptor, kind::f16: D FP32 (bits 4-5 = 1), A and B of one
@@ -87,6 +93,8 @@ struct Args {
   float* upd_w[kMaxBatch];
   void* upd_out[kMaxBatch];
   int32_t* err;
+  int stage;  // d (and dt) 16-byte aligned with pitches in multiples of 8, no df / update: staged stores
+  int upd_stage_out;  // the update's copy 16-byte aligned rows (cols % 8 == 0): staged too
   const int32_t* skip;  // optional device flag: nonzero = return at once (a refused optimizer step)
   FaultPlan fault;  // test-only: a tile whose first k-block is withheld, and the launch's wait bound
 };
@@ -254,6 +262,125 @@ __device__ __forceinline__ void store_chunk(const Args& g, float (&v)[32], int m
   }
 }
 
+// Coalesced load of the 32 x 32 16-bit block at src (row pitch ld) into the
+// warp's staging rows: lane l moves 16 B of rows l/4 + 8i.
+__device__ __forceinline__ void stage_load_block(uint8_t* stg, const uint16_t* src, int64_t ld, int lane) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = (lane >> 2) + 8 * i, c4 = lane & 3;
+    *reinterpret_cast<uint4*>(stg + r * kStageRow + c4 * 16) =
+        *reinterpret_cast<const uint4*>(src + (int64_t)r * ld + c4 * 8);
+  }
+}
+
+// The block of rows row0..row0+31 (lane = row - row0), columns col..col+31,
+// stored through the warp's staging rows: d row-major, and dt (its transpose)
+// with column j of the block as row col + j. Every element of the block is
+// stored (callers use it for full blocks only).
+template <bool kF16>
+__device__ __forceinline__ void store_chunk_staged(const Args& g, const float (&v)[32], uint8_t* stg, int mat,
+                                                   int row0, int col, int lane) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    uint32_t pk[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h)
+      pk[h] = (uint32_t)f2h<kF16>(v[u * 8 + 2 * h]) | ((uint32_t)f2h<kF16>(v[u * 8 + 2 * h + 1]) << 16);
+    *reinterpret_cast<uint4*>(stg + lane * kStageRow + u * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  }
+  __syncwarp();
+  if (g.d != nullptr) {
+    uint16_t* d = g.d + (int64_t)mat * g.sd;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = (lane >> 2) + 8 * i, c4 = lane & 3;
+      *reinterpret_cast<uint4*>(d + (int64_t)(row0 + r) * g.ldd + col + c4 * 8) =
+          *reinterpret_cast<const uint4*>(stg + r * kStageRow + c4 * 16);
+    }
+  }
+  if (g.dt != nullptr) {
+    uint16_t* dt = g.dt + (int64_t)mat * g.sdt;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int j = (lane >> 2) + 8 * i, r8 = (lane & 3) * 8;
+      uint32_t pk[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const uint32_t lo = *reinterpret_cast<const uint16_t*>(stg + (r8 + 2 * h) * kStageRow + j * 2);
+        const uint32_t hi = *reinterpret_cast<const uint16_t*>(stg + (r8 + 2 * h + 1) * kStageRow + j * 2);
+        pk[h] = lo | (hi << 16);
+      }
+      *reinterpret_cast<uint4*>(dt + (int64_t)(col + j) * g.lddt + row0 + r8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  }
+  __syncwarp();  // the staging rows are rewritten by the next block
+}
+
+// The fused Muon update of a full 32 x 32 block of a wide matrix (o[i][j] is
+// w[i][j]; rows row0.., columns col..), through the warp's staging rows: w is
+// read and written back 8 rows x 128 B per instruction, the lane of row r
+// applies w = fma(o * scale, -lr, w * (1 - lr wd)) to its own row in between
+// (the same arithmetic as store_chunk), and the copy leaves 8 rows x 64 B.
+__device__ __forceinline__ void update_chunk_staged(const Args& g, const float (&v)[32], uint8_t* stg, int mat,
+                                                    int row0, int col, int lane) {
+  float* w = g.upd_w[mat] + (int64_t)row0 * g.upd_cols + col;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = (lane >> 3) + 4 * i, c4 = (lane & 7) * 4;
+    *reinterpret_cast<float4*>(stg + r * kStageRowF + c4 * 4) =
+        *reinterpret_cast<const float4*>(w + (int64_t)r * g.upd_cols + c4);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    float4* p = reinterpret_cast<float4*>(stg + lane * kStageRowF + u * 16);
+    float4 x = *p;
+    float rr[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h)
+      rr[h] = __fmaf_rn(__fmul_rn(v[4 * u + h], g.upd_scale), g.upd_neglr, __fmul_rn(rr[h], g.upd_cwd));
+    *p = make_float4(rr[0], rr[1], rr[2], rr[3]);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = (lane >> 3) + 4 * i, c4 = (lane & 7) * 4;
+    *reinterpret_cast<float4*>(w + (int64_t)r * g.upd_cols + c4) =
+        *reinterpret_cast<const float4*>(stg + r * kStageRowF + c4 * 4);
+  }
+  void* out = g.upd_out[mat];
+  if (out != nullptr) {
+    const int64_t base = (int64_t)row0 * g.upd_cols + col;
+    if (g.upd_stage_out) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = (lane >> 2) + 8 * i, c8 = (lane & 3) * 8;
+        const float4 x0 = *reinterpret_cast<const float4*>(stg + r * kStageRowF + c8 * 4);
+        const float4 x1 = *reinterpret_cast<const float4*>(stg + r * kStageRowF + c8 * 4 + 16);
+        const float a[4] = {x0.x, x0.y, x0.z, x0.w}, b[4] = {x1.x, x1.y, x1.z, x1.w};
+        const int64_t e = base + (int64_t)r * g.upd_cols + c8;
+        if (g.upd_odt == MB_BF16) {
+          store4<MB_BF16>(out, e, a);
+          store4<MB_BF16>(out, e + 4, b);
+        } else {
+          store4<MB_F16>(out, e, a);
+          store4<MB_F16>(out, e + 4, b);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float4 x = *reinterpret_cast<const float4*>(stg + lane * kStageRowF + u * 16);
+        const float a[4] = {x.x, x.y, x.z, x.w};
+        const int64_t e = base + (int64_t)lane * g.upd_cols + 4 * u;
+        if (g.upd_odt == MB_BF16) store4<MB_BF16>(out, e, a);
+        else store4<MB_F16>(out, e, a);
+      }
+    }
+  }
+  __syncwarp();  // the staging rows are rewritten by the next block
+}
+
 template <bool kF16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args g) {
@@ -269,6 +396,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain = acc_empty + 2;       // on abort: completion of every MMA issued
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* stage_rows = reinterpret_cast<uint8_t*>(full) + kBarrierBytes;  // 4 x kStageWarp, epilogue warps
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = g.K / BK;
@@ -358,6 +486,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may read
+    uint8_t* stg = stage_rows + (warp - 2) * kStageWarp;
     int it = 0;
     const int total = g.n_tiles * g.batch;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
@@ -370,7 +499,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       int mat, bm, bn;
       tile_coords(g, t, mat, bm, bn);
-      const int row = bm * BM + q * 32 + lane;
+      const int row0 = bm * BM + q * 32;
+      const int row = row0 + lane;
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
         tmem_ld32(tmem + (uint32_t)(a * BN) + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
@@ -384,10 +514,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (col + j == row) v[j] += g.diag;  // compile-time index: v stays in registers
         }
         if (g.c != nullptr) {
-          const uint4* src = reinterpret_cast<const uint4*>(g.c + (int64_t)mat * g.sc + (int64_t)row * g.ldc + col);
+          // the C block through the staging rows: coalesced in, one row per lane out
+          stage_load_block(stg, g.c + (int64_t)mat * g.sc + (int64_t)row0 * g.ldc + col, g.ldc, lane);
+          __syncwarp();
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            uint4 w4 = src[u];
+            uint4 w4 = *reinterpret_cast<const uint4*>(stg + lane * kStageRow + u * 16);
             const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
@@ -395,8 +527,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               v[u * 8 + 2 * h + 1] = fmaf(g.beta, h2f<kF16>((uint16_t)(ww[h] >> 16)), v[u * 8 + 2 * h + 1]);
             }
           }
+          __syncwarp();  // every lane holds its C row: the staging rows may be rewritten
         }
-        store_chunk<kF16>(g, v, mat, row, col);
+        // symmetric outputs: a block entirely above the diagonal is stored whole
+        // (and mirrored through dt), one entirely below is not stored at all
+        const bool upper = row0 + 31 < col, lower = row0 > col + 31;
+        if (g.stage && (!g.sym || upper)) {
+          store_chunk_staged<kF16>(g, v, stg, mat, row0, col, lane);
+        } else if (g.upd && !g.upd_tall && g.upd_vec && row0 + 32 <= g.upd_m && col + 32 <= g.upd_n) {
+          update_chunk_staged(g, v, stg, mat, row0, col, lane);
+        } else if (!(g.sym && lower)) {
+          store_chunk<kF16>(g, v, mat, row, col);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -510,6 +652,10 @@ int gemm16(const GemmCall& q, cudaStream_t stream) {
   }
   g.err = q.err;
   g.skip = q.skip;
+  g.stage = q.d != nullptr && !q.df && !q.upd_w &&
+            (q.dt == nullptr || (aligned(q.dt, 16) && q.lddt % 8 == 0 && q.sdt % 8 == 0));
+  g.upd_stage_out = q.upd_out != nullptr && q.upd_cols % 8 == 0;
+  for (int b = 0; b < q.batch && g.upd_stage_out; ++b) g.upd_stage_out = aligned(q.upd_out[b], 16);
   take_fault(kFaultGemm, &g.fault.unit, &g.fault.limit_ns);
   static int sms = 0;
   if (sms == 0) {
