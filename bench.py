@@ -1119,9 +1119,10 @@ def run_update_only(args, rank, world, local_rank, shapes, sizes):
     for n in sizes:
         a, b = max(off, lo), min(off + n, hi)
         if a < b:
-            o = a - lo
-            eng.slot(w[o:o + b - a], 0)
-            entries.append((w[o:o + b - a], m[o:o + b - a], v[o:o + b - a], g[o:o + b - a], out[o:o + b - a], 0))
+            o, k = a - lo, b - a
+            piece = w[o:o + k]  # the clock slot is keyed by this view object: keep it in the entry
+            eng.slot(piece, 0)
+            entries.append((piece, m[o:o + k], v[o:o + k], g[o:o + k], out[o:o + k], 0))
         off += n
     plan = eng.prepare(entries, [(LR, BETAS[0], BETAS[1], EPS, WD, "torch")], _lib.MB_BF16, _lib.MB_BF16)
     fin = eng.finalize_opts(_lib.MB_FIN_CLIP_TORCH | _lib.MB_FIN_GATE, MAX_NORM)
