@@ -79,3 +79,17 @@ def test_c_caller_links_and_runs(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stderr
     assert "c abi ok" in r.stdout
+
+
+def test_fault_arming_is_host_only_and_validated():
+    """The test-only fault entry arms and disarms on the host without touching
+    a device; it refuses unknown kernels, negative units and bounds outside
+    1 us .. 2 s, and disarming (kernel 0) always succeeds."""
+    L = _lib.lib()
+    assert L.mb_debug_arm_fault(3, 0, 5_000_000) == _lib.MB_ERR_ARG
+    assert L.mb_debug_arm_fault(_lib.MB_FAULT_APPLY, -1, 5_000_000) == _lib.MB_ERR_ARG
+    assert L.mb_debug_arm_fault(_lib.MB_FAULT_STATS, 0, 999) == _lib.MB_ERR_ARG
+    assert L.mb_debug_arm_fault(_lib.MB_FAULT_GEMM, 0, 2_000_000_001) == _lib.MB_ERR_ARG
+    for kernel in (_lib.MB_FAULT_APPLY, _lib.MB_FAULT_STATS, _lib.MB_FAULT_GEMM):
+        assert L.mb_debug_arm_fault(kernel, 7, 5_000_000) == _lib.MB_OK
+    assert L.mb_debug_arm_fault(0, -1, 0) == _lib.MB_OK
