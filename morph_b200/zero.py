@@ -87,12 +87,15 @@ class PeerBuffer:
         handles = [None] * dist.get_world_size(group)
         dist.all_gather_object(handles, bytes(handle), group=group)
         me = dist.get_rank(group)
+        world = len(handles)
         self.peers = []
         try:
             with torch.cuda.device(self.device):
-                for r, h in enumerate(handles):
-                    if r == me:
-                        continue
+                # peers in the order me+1, me+2, ...: a kernel storing to its peers
+                # in list order then starts on a different GPU on every rank, so no
+                # GPU's links receive everyone's first stores at once
+                for k in range(1, world):
+                    h = handles[(me + k) % world]
                     pp = ctypes.c_void_p()
                     _lib.check(lib.mb_ipc_open((ctypes.c_uint8 * 64).from_buffer_copy(h), ctypes.byref(pp)),
                                "mb_ipc_open")
