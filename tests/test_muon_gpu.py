@@ -380,3 +380,37 @@ def test_hybrid_step_replays_from_a_cuda_graph(cuda):
         assert torch.equal(a, b), k
     for i in oa.momentum:
         assert torch.equal(oa.momentum[i], ob.momentum[i])
+
+
+def test_hybrid_gate_over_two_gradient_dtypes(cuda):
+    """BF16 Muon gradients next to FP32 AdamW gradients: the gate sums one
+    record per dtype into one decision. The step equals the one taken with the
+    same values as FP32 everywhere (one dtype), bit for bit, and a NaN in
+    either dtype's group refuses the whole step."""
+    from morph_b200 import HybridMuonAdamW
+
+    def build(muon_dtype):
+        model = _hybrid_model(cuda, 9)
+        for p in model.parameters():
+            if p.dim() == 2:
+                p.grad_dtype = None
+                p.grad = p.grad.to(torch.bfloat16).to(muon_dtype)
+        return model, HybridMuonAdamW(model, lr=.02)
+
+    ma, oa = build(torch.bfloat16)
+    mb, ob = build(torch.float32)
+    assert oa.muon[0].grad.dtype == torch.bfloat16 and ob.muon[0].grad.dtype == torch.float32
+    for _ in range(2):
+        oa.step()
+        ob.step()
+    for (k, a), b in zip(ma.state_dict().items(), mb.state_dict().values()):
+        assert torch.equal(a, b), k
+    for bad in (ma[0].weight, ma[2].weight):  # BF16 Muon group, then FP32 AdamW group
+        before = {k: v.clone() for k, v in ma.state_dict().items()}
+        saved = bad.grad.clone()
+        bad.grad.view(-1)[1] = float("nan")
+        with pytest.raises(FloatingPointError):
+            oa.step()
+        bad.grad.copy_(saved)
+        for k, v in ma.state_dict().items():
+            assert torch.equal(v, before[k]), k
