@@ -41,10 +41,10 @@ LR, BETAS, EPS, WD, MAX_NORM = 3e-4, (0.9, 0.95), 1e-8, 0.1, 1.0
 APPLY_BYTES = 28   # kernel 1: g 2 R + w,m,v 12 R + w,m,v 12 W + BF16 copy 2 W
 STATS_BYTES = 2    # kernel 2: g 2 R
 # Kernel 1's DRAM traffic per parameter, dram__bytes_read.sum + dram__bytes_write.sum
-# from one ncu capture of a one-layer launch (1.321411 GB + 1.263679 GB over
+# from one ncu capture of a one-layer launch (1.321516 GB + 1.262883 GB over
 # 94,384,128 params); traffic grows in proportion to the parameters processed.
 NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (B200, NVLink 5)
-APPLY_TRAFFIC_PER_PARAM = (1.321469e9 + 1.264979e9) / 94384128  # ncu, k_adamw_apply_bulk, one layer
+APPLY_TRAFFIC_PER_PARAM = (1.321516e9 + 1.262883e9) / 94384128  # ncu, k_adamw_apply_bulk, one layer
 FALLBACK_HBM_GBS = 6650.0
 
 
