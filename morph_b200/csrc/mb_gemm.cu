@@ -44,7 +44,15 @@
 namespace mb {
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+// Tuning knob: K depth of a ring stage. 64 (default): 128-byte swizzled
+// K-major tiles, 4 stages; 32: 64-byte swizzled tiles, 8 stages of half the
+// size (the same shared memory, twice the stages in flight).
+#ifndef MB_GEMM_BK
+#define MB_GEMM_BK 64
+#endif
+constexpr int BM = 128, BN = 256, BK = MB_GEMM_BK, STAGES = BK == 64 ? 4 : 8;
+static_assert(BK == 64 || BK == 32, "K stages of 64 or 32 elements");
+constexpr int kRowBytes = BK * 2;  // one K-major row of a stage: the swizzle span
 constexpr int kWarps = 6;
 constexpr int kGemmThreads = kWarps * 32;
 constexpr int A_STAGE = BM * BK * 2;   // 16 KiB
@@ -110,11 +118,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 B apart (SBO), version 1 (bits 46-47), layout type 2 (bits 61-63).
+// Shared-memory matrix descriptor: K-major, rows of kRowBytes swizzled over
+// that span (layout type 2 = 128-byte, 4 = 64-byte swizzle, bits 61-63), 8-row
+// groups 8 * kRowBytes apart (SBO), version 1 (bits 46-47).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+  constexpr uint64_t layout = kRowBytes == 128 ? 2 : 4;
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(8 * kRowBytes >> 4) << 32) |
+         ((uint64_t)1 << 46) | (layout << 61);
 }
 
 __device__ __forceinline__ void umma_16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t id,
@@ -580,7 +590,8 @@ bool make_map(CUtensorMap* map, const void* base, int64_t batch, int64_t rows, i
   cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base),
-            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            kRowBytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
