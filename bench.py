@@ -472,10 +472,11 @@ def run_config4_zero(args, rank, world, local_rank, emit=True):
     from morph_b200.zero import ZeroHybridMuonAdamW
     device = torch.device("cuda", local_rank)
     model = config4_model(device, args.c4_layers)
-    opt = ZeroHybridMuonAdamW(model, lr=3e-4, weight_decay=.1, ns_dtype="bf16", device=device)
+    opt = ZeroHybridMuonAdamW(model, lr=3e-4, weight_decay=.1, ns_dtype="bf16", device=device, sync=False)
     grads = [p.grad for p in model.parameters()]
     for _ in range(args.warmup):
         opt.step(grads)
+    opt.check()
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
@@ -486,6 +487,7 @@ def run_config4_zero(args, rank, world, local_rank, emit=True):
             opt.step(grads)
         stop.record()
         torch.cuda.synchronize()
+    opt.check()  # the device gate's verdict on the last step (every rank reads the same record)
     dist.barrier()
     t = torch.tensor([start.elapsed_time(stop) / args.steps], device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -18,6 +18,9 @@ MB_ERR_CUDA = 3
 MB_ERR_OVERFLOW_MIN_SCALE = 4
 MB_ERR_NONFINITE = 5
 MB_ERR_TIMEOUT = 6
+# a statistics pass that gave up reports its nonfinite count as at least 2^40
+# (mb_adamw.cu kTimeoutMark): the step is refused as a time-out
+TIMEOUT_MARK = float(1 << 40)
 MB_ERR_INDEX = 7
 MB_ERR_UNREPRESENTABLE = 8
 MB_ERR_TOO_LARGE = 9

@@ -24,6 +24,7 @@ the only one this package provides.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 import torch.distributed as dist
@@ -159,8 +160,11 @@ class CudaZeroBackend:
             tiles[r + 1] += tiles[r]
         self._round_tiles = tiles
 
-    def stats(self, fin_flags, max_norm):
+    def finalize_opts(self, fin_flags, max_norm):
         self._fin = self.engine.finalize_opts(fin_flags, max_norm)
+
+    def stats(self, fin_flags, max_norm):
+        self.finalize_opts(fin_flags, max_norm)
         with torch.cuda.device(self.device):
             _lib.check(self.engine.lib.mb_grad_stats(ctypes.byref(self._plan), None, _lib.stream_handle()),
                        "mb_grad_stats")
@@ -189,6 +193,10 @@ class CudaZeroBackend:
         st = self.engine.read_state()
         return dict(norm=float(st.norm), skipped=bool(st.skip), status=int(st.status),
                     clip_coef=float(st.clip_coef))
+
+    def skip_flag(self) -> int:
+        """Device address of the step state's skip flag (kernels read it)."""
+        return self.engine.state_buf.data_ptr() + _lib.StepState.skip.offset
 
 
 class ZeroAdamW:
@@ -264,6 +272,7 @@ class ZeroAdamW:
         self.backend = (backend if backend is not None else
                         CudaZeroBackend(self.device, reserve_sms if self.world > 1 else 0))
         self._keys = [object() for _ in self.pieces]  # one clock slot per piece
+        self._planned = False
 
     def _want_peers(self, peer_writes, backend):
         """Fused update + all-gather (kernel 1 stores the low-precision copies
@@ -312,6 +321,18 @@ class ZeroAdamW:
         (optional, 4 CUDA events) are recorded on the current stream before
         the statistics, after the finalize, after the last update round and
         after the last all-gather."""
+        self.begin(grads, events=events)
+        self.finish(events=events)
+
+    @torch.no_grad()
+    def begin(self, grads, events=None, record=None) -> None:
+        """The first half of ``step``: the plan, the statistics, their all-reduce
+        and the finalize (skip, clip and clocks decided on the device). With
+        ``record`` (2 FP64 on this device: a caller's {sum of squares,
+        nonfinite}, already summed over every rank and covering these
+        gradients), the finalize decides from it instead, with no statistics
+        pass and no all-reduce here, so one decision covers a larger step
+        (ZeroHybridMuonAdamW). ``finish`` must follow on every rank."""
         grads = list(grads)
         if len(grads) != len(self.sizes):
             raise ValueError("one gradient per parameter expected")
@@ -331,22 +352,35 @@ class ZeroAdamW:
             rounds.append(k)
         if events:
             events[0].record()
+        self._planned = bool(entries)
         if entries:
             self.backend.prepare(self._keys, entries, rounds, self.lr, self.betas, self.eps, self.weight_decay,
                                  gdt, self.low_precision)
-            self.backend.stats(self._fin_flags(), self.max_norm)
+            if record is None:
+                self.backend.stats(self._fin_flags(), self.max_norm)
+            else:
+                self.backend.finalize_opts(self._fin_flags(), self.max_norm)
+        if record is not None:
+            if entries:
+                self.backend.record().copy_(record)
         else:
-            self.backend.record().zero_()
-        if self.world > 1:
-            dist.all_reduce(self.backend.record(), group=self.group)
+            if not entries:
+                self.backend.record().zero_()
+            if self.world > 1:
+                dist.all_reduce(self.backend.record(), group=self.group)
         if entries:
             self.backend.finalize()
         if events:
             events[1].record()
+
+    @torch.no_grad()
+    def finish(self, events=None) -> None:
+        """The second half of ``step``: the update rounds (each launch first reads
+        the skip flag) and the all-gather of the low-precision weights."""
         works = []
         deltas = self._peer.deltas if self._peer is not None else None
         for k in range(self.rounds):
-            if entries:
+            if self._planned:
                 self.backend.apply_round(k, deltas) if deltas else self.backend.apply_round(k)
             if self.world > 1 and deltas is None:
                 works.append(self._gather(k))
@@ -361,6 +395,15 @@ class ZeroAdamW:
             events[3].record()
         if self.sync:
             self.check()
+
+    def skip_flag(self):
+        """The backend's handle on this step's device skip flag (set by
+        ``begin``), or None when this rank holds no piece of the group."""
+        return self.backend.skip_flag() if self._planned else None
+
+    def record(self) -> torch.Tensor:
+        """The step's all-reduced {sum of squares, nonfinite} record."""
+        return self.backend.record()
 
     def check(self) -> None:
         """Wait for the last step and raise FloatingPointError if it was refused."""
@@ -412,6 +455,8 @@ class CudaHybridBackend:
         self.ns_dtype = ns_dtype
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._keys = {}
+        self._plan = None
+        self._fin = self.engine.finalize_opts(_lib.MB_FIN_GATE, None)
 
     def gate_record(self, grads) -> torch.Tensor:
         """Kernel 2 over ``grads``: the {sumsq, nonfinite} record (2 x FP64 on the device)."""
@@ -431,13 +476,31 @@ class CudaHybridBackend:
                                    keys=keys)
         with torch.cuda.device(self.device):
             _lib.check(self.engine.lib.mb_grad_stats(ctypes.byref(plan), None, _lib.stream_handle()), "mb_grad_stats")
+        self._plan = plan
         return rec
 
-    def muon_batch(self, params, moms, grads, outs, lr, weight_decay):
+    def gate_finalize(self, record):
+        """The finiteness gate (optimizer.py:50-51) decided on the device from
+        ``record`` (the all-reduced {sumsq, nonfinite}): returns the device
+        address of the skip flag every Muon launch reads, or None when this
+        rank has computed no statistics yet (it then launches no Muon kernel)."""
+        if self._plan is None:
+            return None
+        rec = self.engine.state_buf[:16].view(torch.float64)
+        if rec.data_ptr() != record.data_ptr():
+            rec.copy_(record)
+        with torch.cuda.device(self.device):
+            _lib.check(self.engine.lib.mb_step_finalize(ctypes.byref(self._plan), ctypes.byref(self._fin),
+                                                        _lib.stream_handle()), "mb_step_finalize")
+        return self.engine.state_buf.data_ptr() + _lib.StepState.skip.offset
+
+    def muon_batch(self, params, moms, grads, outs, lr, weight_decay, skip=None):
+        """One kernel-4 step over a batch; ``skip``: device address of a skip flag."""
         from .muon import muon_step_batched
-        muon_step_batched(params, moms, grads, outs, lr, weight_decay, self.ns_dtype, self.err)
+        muon_step_batched(params, moms, grads, outs, lr, weight_decay, self.ns_dtype, self.err, skip)
 
     def check_errors(self):
+        """Raise RuntimeError if a bounded wait of a Muon launch expired (waits for the stream)."""
         if int(self.err.item()):
             self.err.zero_()
             raise RuntimeError("muon step: a bounded wait expired on the device")
@@ -452,23 +515,29 @@ class ZeroHybridMuonAdamW:
     Rank r keeps the FP32 masters and momentum of its matrices; the AdamW group
     (embedding, norms, biases) is a ``ZeroAdamW`` over the flat space. Every rank
     holds the full low-precision weights (``weights``, one tensor per parameter
-    in ``params`` order). One step:
+    in ``params`` order). One step, enqueued without a host read:
 
       1. kernel 2 (finiteness) over this rank's Muon gradients and its AdamW
-         chunks; all_reduce of the 16-byte record; every rank raises
-         FloatingPointError, changing nothing, if any gradient is not finite
-         (optimizer.py:50-51);
-      2. per round: this rank's batch of one shape through kernel 4, writing the
-         BF16 copies into place, then all_gather_into_tensor of the round's
-         block (in place, on NCCL's stream) while the next round computes;
-      3. the AdamW group's ZeRO-1 step (kernels 2 + 1, its own all-gathers).
+         chunks; all_reduce of the 16-byte record; the one-block finalize
+         decides the gate on the device (optimizer.py:50-51);
+      2. per round: this rank's batch of one shape through kernel 4 (every
+         launch reads the skip flag first), writing the BF16 copies into place,
+         then all_gather_into_tensor of the round's block (in place, on NCCL's
+         stream) while the next round computes;
+      3. the AdamW group's ZeRO-1 step, finalized from the same record (no
+         second statistics pass or all-reduce; kernel 1 and its all-gathers).
+
+    A refused step changes nothing on any rank (the all-gathers carry the
+    unchanged weights). With ``sync=True`` (the default, the reference's
+    behaviour) ``step`` then raises FloatingPointError on every rank; with
+    ``sync=False`` it only enqueues and ``check()`` raises later.
 
     ``params`` are the model's parameters; ``muon`` selects the Muon ones
     (default: ``partition(model)`` when ``model`` is given)."""
 
     def __init__(self, model=None, lr=1e-3, muon_lr=None, weight_decay=.01, *, params=None, muon=None,
                  low_precision=torch.bfloat16, process_group=None, device=None, backend=None, adam_backend=None,
-                 ns_dtype="auto", workspace_limit=4 << 30, adam_rounds=4):
+                 ns_dtype="auto", workspace_limit=4 << 30, adam_rounds=4, sync=True):
         from .muon import batch_plan, partition
         if model is not None:
             muon_list, adam_list = partition(model)
@@ -487,6 +556,7 @@ class ZeroHybridMuonAdamW:
         self.lr = lr if muon_lr is None else muon_lr
         self.weight_decay = weight_decay
         self.low_precision = low_precision
+        self.sync = bool(sync)
         self.params = params
         self.muon = muon_list
         self.adam_params = adam_list
@@ -519,11 +589,14 @@ class ZeroHybridMuonAdamW:
         self.owned = [i for rd in self.rounds for i in rd[self.rank]]
         self.master = {i: self.muon[i].detach().to(self.device, torch.float32).clone() for i in self.owned}
         self.momentum = {}
+        self._new_momentum = []
+        self._record = torch.zeros(2, dtype=torch.float64, device=self.device)
         for i in range(len(self.muon)):  # every rank starts from the full weights
             self.muon_weights[i].copy_(self.muon[i].detach().to(self.device))
-        self.adam = ZeroAdamW(adam_list, lr=lr, betas=(.9, .95), eps=1e-8, weight_decay=weight_decay,
-                              low_precision=low_precision, process_group=process_group, device=self.device,
-                              backend=adam_backend, rounds=adam_rounds) if adam_list else None
+        # the AdamW group finalizes from the gate's all-reduced record (gate on, no host read)
+        self.adam = ZeroAdamW(adam_list, lr=lr, betas=(.9, .95), eps=1e-8, weight_decay=weight_decay, gate=True,
+                              sync=False, low_precision=low_precision, process_group=process_group,
+                              device=self.device, backend=adam_backend, rounds=adam_rounds) if adam_list else None
         index = {id(p): i for i, p in enumerate(self.muon)}
         aindex = {id(p): i for i, p in enumerate(adam_list)}
         self.weights = [self.muon_weights[index[id(p)]] if id(p) in index else self.adam.weights[aindex[id(p)]]
@@ -557,32 +630,53 @@ class ZeroHybridMuonAdamW:
         by_dtype = {}
         for g in own_grads:
             by_dtype.setdefault(g.dtype, []).append(g)
-        rec = torch.zeros(2, dtype=torch.float64, device=self.device)
+        rec = self._record
+        rec.zero_()
         for gs in by_dtype.values():
             rec += self.backend.gate_record(gs)
         if self.world > 1:
             dist.all_reduce(rec, group=self.group)
-        if float(rec[1].item()) != 0.0:
-            raise FloatingPointError('nonfinite gradient; optimizer not updated')
-        self.backend.check_errors()
+        skip = self.backend.gate_finalize(rec)
         # 2. Muon rounds, each all-gathered while the next computes
         works = []
+        self._new_momentum = []
         for k, rd in enumerate(self.rounds):
             mine = rd[self.rank]
             if mine:
                 for i in mine:
                     if i not in self.momentum:
                         self.momentum[i] = torch.zeros_like(self.master[i])
+                        self._new_momentum.append(i)
                 self.backend.muon_batch([self.master[i] for i in mine], [self.momentum[i] for i in mine],
                                         [muon_grads[i] for i in mine], [self.muon_weights[i] for i in mine],
-                                        self.lr, self.weight_decay)
+                                        self.lr, self.weight_decay, skip)
             if self.world > 1:
                 works.append(self._gather(k))
-        # 3. the AdamW group
+        # 3. the AdamW group, finalized from the same record
         if self.adam is not None:
-            self.adam.step(adam_grads)
+            self.adam.begin(adam_grads, record=rec)
+            self.adam.finish()
         for w in works:
             w.wait()
+        if self.sync:
+            self.check()
+
+    def check(self) -> None:
+        """Wait for the last step and raise what it reported: RuntimeError if a
+        bounded device wait expired, FloatingPointError if the gate refused the
+        step (nothing changed; momentum buffers it created are dropped, as the
+        reference never creates them). Every rank reads the same all-reduced
+        record, so every rank raises alike."""
+        self.backend.check_errors()
+        sumsq, bad = (float(x) for x in self._record.cpu())
+        if bad >= _lib.TIMEOUT_MARK:
+            raise RuntimeError("gradient statistics: a bounded wait expired on the device")
+        if bad != 0.0 or not math.isfinite(sumsq):
+            for i in self._new_momentum:
+                self.momentum.pop(i, None)
+            self._new_momentum = []
+            raise FloatingPointError('nonfinite gradient; optimizer not updated')
+        self._new_momentum = []
 
     def close(self):
         """Release the AdamW group's peer-mapped buffer (collective)."""

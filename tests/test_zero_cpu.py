@@ -38,6 +38,9 @@ class OracleBackend:
     def prepare(self, keys, entries, rounds, lr, betas, eps, weight_decay, grad_dtype, out_dtype):
         self.entries, self.rounds, self.hyper = entries, rounds, (lr, betas, eps, weight_decay)
 
+    def finalize_opts(self, fin_flags, max_norm):
+        pass  # the double always gates and clips with its own max_norm
+
     def stats(self, fin_flags, max_norm):
         from oracle import oracle as orc
         total, bad = 0.0, 0

@@ -38,9 +38,15 @@ class OracleHybridBackend:
     def batch_plan(n, rows, cols):
         return [2] * (n // 2) + ([n % 2] if n % 2 else [])
 
-    def muon_batch(self, params, moms, grads, outs, lr, weight_decay):
+    def gate_finalize(self, record):
+        """The skip decision as a one-element tensor (the device flag's stand-in)."""
+        return torch.tensor([int(float(record[1]) != 0.0)], dtype=torch.int32)
+
+    def muon_batch(self, params, moms, grads, outs, lr, weight_decay, skip=None):
         from oracle import oracle as orc
         assert len({tuple(p.shape) for p in params}) == 1
+        if skip is not None and int(skip[0]):
+            return  # the kernels read the flag first and change nothing
         for p, m, g, o in zip(params, moms, grads, outs):
             u = orc.muon_momentum_(m.numpy(), g.float().numpy())
             orc.muon_apply_(p.numpy(), orc.orthogonalize(u), lr, weight_decay)
@@ -71,27 +77,31 @@ def _grads(model, steps=3, poison=None):
     return out
 
 
-def _run(poison=None):
+def _run(poison=None, sync=True):
+    """Three steps; with sync=False a refused step is reported by check()
+    after it was enqueued, and the next step still proceeds."""
     model = _model()
     opt = ZeroHybridMuonAdamW(model, lr=LR, weight_decay=WD, device="cpu", backend=OracleHybridBackend(),
-                              adam_backend=OracleBackend(None), adam_rounds=2)
+                              adam_backend=OracleBackend(None), adam_rounds=2, sync=sync)
     raised = []
     for s, gs in enumerate(_grads(model, poison=poison)):
         try:
             opt.step(gs)
+            if not sync:
+                opt.check()
         except FloatingPointError:
             raised.append(s)
     masters = {i: t.clone() for i, t in opt.master.items()}
     weights = [w.float().clone() for w in opt.weights]
-    return masters, weights, raised, [sorted(rd[opt.rank]) for rd in opt.rounds]
+    return masters, weights, raised, [sorted(rd[opt.rank]) for rd in opt.rounds], sorted(opt.momentum)
 
 
-def _worker(rank, world, port, q, poison):
+def _worker(rank, world, port, q, poison, sync):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        q.put((rank, to_host(_run(poison))))
+        q.put((rank, to_host(_run(poison, sync))))
     finally:
         dist.destroy_process_group()
 
@@ -102,11 +112,11 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _two_ranks(poison=None):
+def _two_ranks(poison=None, sync=True):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, poison)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, poison, sync)) for r in range(2)]
     for p in procs:
         p.start()
     results = {r: from_host(v) for r, v in (q.get(timeout=180) for _ in procs)}
@@ -136,10 +146,10 @@ def test_deal_matrices_balances_each_shape():
 
 def test_two_gloo_ranks_equal_one_rank():
     results = _two_ranks()
-    single_masters, single_weights, raised, _ = _run()
+    single_masters, single_weights, raised, _, _ = _run()
     assert raised == []
-    m0, w0, r0, own0 = results[0]
-    m1, w1, r1, own1 = results[1]
+    m0, w0, r0, own0, _ = results[0]
+    m1, w1, r1, own1, _ = results[1]
     assert r0 == r1 == []
     assert not set(m0) & set(m1) and set(m0) | set(m1) == set(single_masters)  # each matrix on one rank
     for i, t in {**m0, **m1}.items():
@@ -152,15 +162,20 @@ def test_two_gloo_ranks_equal_one_rank():
         assert torch.equal(a, c)
 
 
-def test_nonfinite_gradient_raises_on_every_rank_and_changes_nothing():
+@pytest.mark.parametrize("sync", [True, False])
+def test_nonfinite_gradient_raises_on_every_rank_and_changes_nothing(sync):
+    """The gate decides on the device from the all-reduced record: the Muon
+    launches and the AdamW group skip, the all-gathers carry unchanged weights,
+    and every rank raises (inside step with sync=True, from check() with
+    sync=False)."""
     # step 1 poisons the first Muon matrix (parameter index 1: after the embedding)
-    results = _two_ranks(poison=(1, 1))
-    clean_masters, clean_weights, _, _ = _run()
+    results = _two_ranks(poison=(1, 1), sync=sync)
+    clean_masters, clean_weights, _, _, _ = _run()
     for rank in (0, 1):
-        masters, weights, raised, _ = results[rank]
+        masters, weights, raised, _, _ = results[rank]
         assert raised == [1]
     # steps 0 and 2 applied, step 1 skipped: equals a 1-rank run with the same poison
-    single_masters, single_weights, raised, _ = _run(poison=(1, 1))
+    single_masters, single_weights, raised, _, _ = _run(poison=(1, 1))
     assert raised == [1]
     for rank in (0, 1):
         for i, t in results[rank][0].items():
@@ -168,3 +183,21 @@ def test_nonfinite_gradient_raises_on_every_rank_and_changes_nothing():
         for a, c in zip(results[rank][1], single_weights):
             assert torch.equal(a, c)
     assert any(not torch.equal(a, c) for a, c in zip(single_weights, clean_weights))
+
+
+def test_refused_first_step_creates_no_momentum():
+    """A step refused before any Muon momentum existed leaves none behind
+    (the reference raises before creating it); the next step creates it."""
+    model = _model()
+    opt = ZeroHybridMuonAdamW(model, lr=LR, weight_decay=WD, device="cpu", backend=OracleHybridBackend(),
+                              adam_backend=OracleBackend(None), adam_rounds=2, sync=False)
+    before = [w.float().clone() for w in opt.weights]
+    grads = _grads(model, poison=(0, 1))
+    opt.step(grads[0])
+    with pytest.raises(FloatingPointError):
+        opt.check()
+    assert opt.momentum == {}
+    assert all(torch.equal(a.float(), b) for a, b in zip(opt.weights, before))
+    opt.step(grads[1])
+    opt.check()
+    assert sorted(opt.momentum) == sorted(opt.master)

@@ -1,7 +1,8 @@
 """Sharded Hybrid Muon + AdamW on the GPU: on one GPU it equals
-HybridMuonAdamW bit for bit (same kernels, same batches); on 2 GPUs (NCCL, one
-process per GPU) every rank holds the same gathered weights, equal to the
-1-GPU run, and each Muon master lives on exactly one rank."""
+HybridMuonAdamW bit for bit (same kernels, same batches), refused steps
+included; on 2 GPUs (NCCL, one process per GPU) every rank holds the same
+gathered weights, equal to the 1-GPU run, each Muon master lives on exactly one
+rank, and a nonfinite gradient in one rank's share refuses the step on both."""
 import datetime
 import os
 import socket
@@ -28,36 +29,61 @@ def _model(device):
         torch.nn.LayerNorm(256)).to(device)
 
 
-def _grads(model, device, steps=3):
+# (step, parameter index) of a NaN: parameter 2 is Muon matrix 1, which rank 1 holds on 2 GPUs
+POISON = (2, 2)
+
+
+def _grads(model, device, steps=3, poison=None):
     g = torch.Generator().manual_seed(13)
-    return [[(torch.randn(p.shape, generator=g) * 1e-2).to(torch.bfloat16).to(device) for p in model.parameters()]
-            for _ in range(steps)]
+    out = []
+    for s in range(steps):
+        gs = [(torch.randn(p.shape, generator=g) * 1e-2).to(torch.bfloat16) for p in model.parameters()]
+        if poison is not None and s == poison[0]:
+            gs[poison[1]].view(-1)[7] = float("nan")
+        out.append([x.to(device) for x in gs])
+    return out
 
 
-def _run_zero(device):
+def _run_zero(device, poison=None, steps=3, sync=True):
     from morph_b200.zero import ZeroHybridMuonAdamW
     model = _model(device)
-    opt = ZeroHybridMuonAdamW(model, lr=LR, weight_decay=WD, device=device)
-    for gs in _grads(model, device):
-        opt.step(gs)
+    opt = ZeroHybridMuonAdamW(model, lr=LR, weight_decay=WD, device=device, sync=sync)
+    raised = []
+    for s, gs in enumerate(_grads(model, device, steps, poison)):
+        try:
+            opt.step(gs)
+            if not sync:
+                opt.check()
+        except FloatingPointError:
+            raised.append(s)
     torch.cuda.synchronize(device)
     out = ({i: t.cpu() for i, t in opt.master.items()}, [w.cpu() for w in opt.weights],
-           {i: t.cpu() for i, t in opt.momentum.items()})
+           {i: t.cpu() for i, t in opt.momentum.items()}, raised)
     opt.close()
     return out
 
 
-def test_one_gpu_equals_hybrid(cuda):
+@pytest.mark.parametrize("poison,sync", [(None, True), ((0, 1), True), (POISON, False)])
+def test_one_gpu_equals_hybrid(cuda, poison, sync):
+    """Same bits as HybridMuonAdamW; a refused step (first step: no momentum
+    is left behind) raises in step() or, with sync=False, in check()."""
     from morph_b200 import HybridMuonAdamW
-    masters, weights, moms = _run_zero(cuda)
+    steps = 4 if poison else 3
+    masters, weights, moms, raised = _run_zero(cuda, poison, steps, sync)
     model = _model(cuda)
     for p in model.parameters():
         p.grad_dtype = None
     opt = HybridMuonAdamW(model, lr=LR, weight_decay=WD, low_precision=torch.bfloat16)
-    for gs in _grads(model, cuda):
+    ref_raised = []
+    for s, gs in enumerate(_grads(model, cuda, steps, poison)):
         for p, g in zip(model.parameters(), gs):
             p.grad = g
-        opt.step()
+        try:
+            opt.step()
+        except FloatingPointError:
+            ref_raised.append(s)
+    assert raised == ref_raised == ([poison[0]] if poison else [])
+    assert sorted(moms) == sorted(opt.momentum)
     for i, p in enumerate(opt.muon):
         assert torch.equal(masters[i], p.detach().cpu()), i
         assert torch.equal(moms[i], opt.momentum[i].cpu()), i
@@ -73,7 +99,7 @@ def _worker(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        q.put((rank, to_host(_run_zero(torch.device("cuda", rank)))))
+        q.put((rank, to_host(_run_zero(torch.device("cuda", rank), POISON, 4))))
     finally:
         dist.destroy_process_group()
 
@@ -93,9 +119,10 @@ def test_two_gpus_equal_one_gpu(cuda):
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    single_m, single_w, _ = _run_zero(cuda)
-    m0, w0, _ = results[0]
-    m1, w1, _ = results[1]
+    single_m, single_w, _, single_r = _run_zero(cuda, POISON, 4)
+    m0, w0, _, r0 = results[0]
+    m1, w1, _, r1 = results[1]
+    assert r0 == r1 == single_r == [POISON[0]]  # rank 0 holds no NaN, yet refuses too
     assert not set(m0) & set(m1) and set(m0) | set(m1) == set(single_m)
     for i, t in {**m0, **m1}.items():
         assert torch.equal(t, single_m[i]), i
