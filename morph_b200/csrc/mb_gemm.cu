@@ -22,6 +22,15 @@
 // While the epilogue drains tile i from one accumulator, the MMAs of tile
 // i + 1 fill the other.
 //
+// Pair mode (MB_GEMM_PAIR=1 in the environment, M % 256 == 0): clusters of two
+// CTAs on two SMs share one 256 x 256 output tile through tcgen05.mma
+// .cta_group::2 (M = 256). Each CTA loads its own 128 rows of A and 128 of the
+// 256 rows of B (no multicast), so an SM moves 32 KiB per 64-deep k-block
+// instead of 48 KiB; the even CTA issues the MMAs and its commits arrive on
+// both CTAs' barriers; each CTA's TMEM holds its 128 rows of the accumulator
+// and its own epilogue drains them. The odd CTA's loads and epilogue signal the
+// even CTA's barriers through their cluster addresses.
+//
 // Symmetric mode (the output is known symmetric, e.g. X X^T and polynomials
 // of it): only tiles not entirely below the diagonal are computed; elements on
 // or above the diagonal are stored directly and those strictly above are also
@@ -36,6 +45,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "mb_async.cuh"
@@ -66,14 +76,20 @@ constexpr int kStageRowF = 144;  // the fused update's FP32 rows: 128 B + 16 B p
 constexpr int kStageWarp = 32 * kStageRowF;
 constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + 1024 + kBarrierBytes + 4 * kStageWarp;
 constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
+// pair mode: each CTA holds 128 of the tile's 256 B rows, so a stage is 32 KiB
+// (BK = 64) and the same shared memory holds more stages
+constexpr int B_STAGE_P = BM * BK * 2;
+constexpr int STAGES_P = STAGES * (A_STAGE + B_STAGE) / (A_STAGE + B_STAGE_P);
+static_assert(STAGES_P * (A_STAGE + B_STAGE_P) == STAGES * (A_STAGE + B_STAGE), "pair stages fill the same ring");
+static_assert(2 * 8 * STAGES_P + 5 * 8 + 8 <= kBarrierBytes, "barrier area");
 
 // Instruction descriptor, kind::f16: D FP32 (bits 4-5 = 1), A and B of one
 // 16-bit type (bits 7-9 and 10-12: 1 = BF16, 0 = FP16), both K-major (bits 15,
 // 16 = 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
-template <bool kF16>
+template <bool kF16, int kM = BM>
 __host__ __device__ constexpr uint32_t idesc() {
   return (1u << 4) | ((kF16 ? 0u : 1u) << 7) | ((kF16 ? 0u : 1u) << 10) | ((uint32_t)(BN >> 3) << 17) |
-         ((uint32_t)(BM >> 4) << 24);
+         ((uint32_t)(kM >> 4) << 24);
 }
 
 struct Args {
@@ -115,6 +131,66 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Pair mode: the same load, completing on the barrier at cluster address `bar`
+// (the even CTA's); no multicast.
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Cluster address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_u32(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// Every thread of both CTAs of the pair (no early exits may precede it); the
+// non-.aligned form, as the roles reach it from divergent branches.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait for a barrier that the other CTA of the pair also arrives on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > limit_ns) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -152,6 +228,35 @@ __device__ __forceinline__ uint16_t f2h(float x) {
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// Pair mode: one M = 256 MMA over both CTAs (A rows and B rows at the same
+// shared offsets in each), accumulating into both CTAs' TMEM.
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t id,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(id), "r"(accumulate)
+      : "memory");
+}
+
+// Pair mode: arrive on this CTA's barrier `bar` once the pair MMAs issued so
+// far complete.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// ... on the barrier at the same offset in both CTAs of the pair (the commit's
+// cluster-multicast form, CTA mask 0b11; an arrival, not a load).
+__device__ __forceinline__ void umma_commit_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -391,47 +496,86 @@ __device__ __forceinline__ void update_chunk_staged(const Args& g, const float (
   __syncwarp();  // the staging rows are rewritten by the next block
 }
 
-template <bool kF16>
+// Pair mode: tile t -> (matrix, bm, bn) of 256 x 256 tiles (bm fastest);
+// symmetric: column bn holds the tiles bm <= bn.
+__device__ __forceinline__ void tile_coords_pair(const Args& g, int tb, int& mat, int& bm, int& bn) {
+  mat = tb / g.n_tiles;
+  const int t = tb - mat * g.n_tiles;
+  const int mt = g.M / (2 * BM);
+  if (!g.sym) {
+    bm = t % mt;
+    bn = t / mt;
+    return;
+  }
+  int c = 0;
+  for (bn = 0;; ++bn) {
+    const int h = mt < bn + 1 ? mt : bn + 1;
+    if (t < c + h) {
+      bm = t - c;
+      return;
+    }
+    c += h;
+  }
+}
+
+template <bool kF16, bool kPair>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args g) {
+  constexpr int ST = kPair ? STAGES_P : STAGES;
+  constexpr int B_ST = kPair ? B_STAGE_P : B_STAGE;
+  // both CTAs of a pair read the same flag, written before this launch: they return together
   if (g.skip != nullptr && *g.skip != 0) return;  // before any barrier or TMEM allocation
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_STAGE;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE);
-  uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = empty + STAGES;   // [2]: MMA -> epilogue
-  uint64_t* acc_empty = acc_full + 2;    // [2]: epilogue -> MMA (4 arrivals: one per epilogue warp)
+  uint8_t* sB = smem + ST * A_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + ST * B_ST);
+  uint64_t* empty = full + ST;
+  uint64_t* acc_full = empty + ST;       // [2]: MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;    // [2]: epilogue -> MMA (one arrival per epilogue warp, both CTAs in pairs)
   uint64_t* drain = acc_empty + 2;       // on abort: completion of every MMA issued
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint8_t* stage_rows = reinterpret_cast<uint8_t*>(full) + kBarrierBytes;  // 4 x kStageWarp, epilogue warps
+  uint8_t* stage_rows = reinterpret_cast<uint8_t*>(smem + ST * (A_STAGE + B_ST)) + kBarrierBytes;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = g.K / BK;
+  // pair mode: CTA rank in the pair, the pair's index and count
+  const uint32_t rank = kPair ? cluster_rank() : 0;
+  const int unit = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int n_units = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const bool leader = rank == 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], kPair ? 8 : 4);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (kPair) {
+      // one warp of each CTA of the pair allocates together: the same columns in both
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) cluster_sync();  // both CTAs' barriers exist before either signals the other's
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -439,56 +583,77 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       int kit = 0;  // k-blocks issued so far (the ring runs on across tiles)
       const int total = g.n_tiles * g.batch;
-      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+      for (int t = unit; t < total && !*abort_flag; t += n_units) {
         int mat, bm, bn;
-        tile_coords(g, t, mat, bm, bn);
+        if constexpr (kPair) tile_coords_pair(g, t, mat, bm, bn);
+        else tile_coords(g, t, mat, bm, bn);
         for (int kb = 0; kb < KB; ++kb, ++kit) {
-          const int s = kit % STAGES;
-          const uint32_t round = kit / STAGES;
+          const int s = kit % ST;
+          const uint32_t round = kit / ST;
           if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, g.fault.limit_ns)) break;
           if (t == g.fault.unit && kb == 0) continue;  // test-only: withhold; the MMA warp's wait expires
-          mbar_expect_tx(&full[s], A_STAGE + B_STAGE);
-          tma_load_3d(sA + s * A_STAGE, &tmA, &full[s], kb * BK, bm * BM, mat);
-          tma_load_3d(sB + s * B_STAGE, &tmB, &full[s], kb * BK, bn * BN, mat);
+          if constexpr (kPair) {
+            // both CTAs' loads complete on the even CTA's barrier, which expects the bytes of both
+            const uint32_t bar = mapa_u32(smem_u32(&full[s]), 0);
+            if (leader) mbar_expect_tx(&full[s], 2 * (A_STAGE + B_ST));
+            tma_load_3d_pair(sA + s * A_STAGE, &tmA, bar, kb * BK, bm * 2 * BM + (int)rank * BM, mat);
+            tma_load_3d_pair(sB + s * B_ST, &tmB, bar, kb * BK, bn * BN + (int)rank * BM, mat);
+          } else {
+            mbar_expect_tx(&full[s], A_STAGE + B_STAGE);
+            tma_load_3d(sA + s * A_STAGE, &tmA, &full[s], kb * BK, bm * BM, mat);
+            tma_load_3d(sB + s * B_STAGE, &tmB, &full[s], kb * BK, bn * BN, mat);
+          }
         }
       }
-      if (*abort_flag) {
-        // Bounded wait for this CTA's own loads still in flight.
+      if (*abort_flag && (!kPair || leader)) {
+        // Bounded wait for the loads still in flight (in pairs, both CTAs' land on the even CTA's barriers).
         const uint64_t t0 = globaltimer();
-        for (int k = kit - STAGES > 0 ? kit - STAGES : 0; k < kit; ++k) {
-          const int s = k % STAGES;
-          const uint32_t round = k / STAGES;
+        for (int k = kit - ST > 0 ? kit - ST : 0; k < kit; ++k) {
+          const int s = k % ST;
+          const uint32_t round = k / ST;
           while (!mbar_try_wait(&full[s], round & 1) && globaltimer() - t0 < g.fault.limit_ns) {
           }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int kit = 0, it = 0;
       const int total = g.n_tiles * g.batch;
-      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++it) {
+      for (int t = unit; t < total && !*abort_flag; t += n_units, ++it) {
         const int a = it & 1;
         const uint32_t use = it >> 1;
-        if (!mbar_wait(&acc_empty[a], (use & 1) ^ 1, abort_flag, g.fault.limit_ns)) break;
+        const bool free_acc = kPair ? mbar_wait_cluster(&acc_empty[a], (use & 1) ^ 1, abort_flag, g.fault.limit_ns)
+                                    : mbar_wait(&acc_empty[a], (use & 1) ^ 1, abort_flag, g.fault.limit_ns);
+        if (!free_acc) break;
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(a * BN);
         for (int kb = 0; kb < KB; ++kb, ++kit) {
-          const int s = kit % STAGES;
-          const uint32_t round = kit / STAGES;
+          const int s = kit % ST;
+          const uint32_t round = kit / ST;
           if (!mbar_wait(&full[s], round & 1, abort_flag, g.fault.limit_ns)) break;
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + s * A_STAGE), b0 = smem_u32(sB + s * B_STAGE);
+          const uint32_t a0 = smem_u32(sA + s * A_STAGE), b0 = smem_u32(sB + s * B_ST);
+          if constexpr (kPair) {
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma_16(acc, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc<kF16>(), (kb | k) != 0 ? 1u : 0u);
-          umma_commit(&empty[s]);
+            for (int k = 0; k < BK / 16; ++k)
+              umma_pair(acc, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc<kF16, 2 * BM>(),
+                        (kb | k) != 0 ? 1u : 0u);
+            umma_commit_both(&empty[s]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              umma_16(acc, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc<kF16>(), (kb | k) != 0 ? 1u : 0u);
+            umma_commit(&empty[s]);
+          }
         }
-        umma_commit(&acc_full[a]);
+        if constexpr (kPair) umma_commit_both(&acc_full[a]);
+        else umma_commit(&acc_full[a]);
       }
       if (*abort_flag) {
         // every MMA this thread issued completes (bounded) before the accumulators are freed
-        umma_commit(drain);
+        if constexpr (kPair) umma_commit_pair(drain);
+        else umma_commit(drain);
         const uint64_t t0 = globaltimer();
         while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < g.fault.limit_ns) {
         }
@@ -499,7 +664,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* stg = stage_rows + (warp - 2) * kStageWarp;
     int it = 0;
     const int total = g.n_tiles * g.batch;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+    for (int t = unit; t < total; t += n_units, ++it) {
       const int a = it & 1;
       const uint32_t use = it >> 1;
       int ok = 0;
@@ -508,8 +673,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ok) break;
       tc_fence_after();
       int mat, bm, bn;
-      tile_coords(g, t, mat, bm, bn);
-      const int row0 = bm * BM + q * 32;
+      if constexpr (kPair) tile_coords_pair(g, t, mat, bm, bn);
+      else tile_coords(g, t, mat, bm, bn);
+      // this CTA's 128 rows of the tile (in pairs, the odd CTA holds rows 128..255)
+      const int row0 = (kPair ? bm * 2 * BM + (int)rank * BM : bm * BM) + q * 32;
       const int row = row0 + lane;
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
@@ -552,14 +719,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      if (lane == 0) {
+        if constexpr (kPair) mbar_arrive_cluster(mapa_u32(smem_u32(&acc_empty[a]), 0));
+        else mbar_arrive(&acc_empty[a]);
+      }
     }
   }
   tc_fence_before();
-  __syncthreads();
+  // pairs: neither CTA leaves (freeing shared memory that the pair's MMAs and
+  // loads use) before the other is done; every wait before this is bounded
+  if constexpr (kPair) cluster_sync();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    if constexpr (kPair)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
   if (threadIdx.x == 0 && *abort_flag && g.err != nullptr) atomicExch(g.err, 1);
 }
@@ -595,6 +771,16 @@ bool make_map(CUtensorMap* map, const void* base, int64_t batch, int64_t rows, i
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Pair mode is opt-in while it is measured: MB_GEMM_PAIR=1 in the environment
+// (read once per process).
+bool pair_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("MB_GEMM_PAIR");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
+
 }  // namespace gemm
 
 int gemm16(const GemmCall& q, cudaStream_t stream) {
@@ -625,23 +811,32 @@ int gemm16(const GemmCall& q, cudaStream_t stream) {
   // symmetric mode writes the lower triangle through dt == d (square output, no other outputs)
   if (q.sym && (M != N || !q.d || q.dt != q.d || q.lddt != q.ldd || q.sdt != q.sd || q.df || q.upd_w))
     return MB_ERR_ARG;
+  // pair mode (opt-in): 256-row tiles over CTA pairs
+  const bool pair = pair_enabled() && M % (2 * BM) == 0;
   CUtensorMap ma, mbm;
   if (!make_map(&ma, q.a, q.batch, M, K, q.lda, q.sa, BM, f16) ||
-      !make_map(&mbm, q.b, q.batch, N, K, q.ldb, q.sb, BN, f16))
+      !make_map(&mbm, q.b, q.batch, N, K, q.ldb, q.sb, pair ? BM : BN, f16))
     return MB_ERR_CUDA;
   static std::once_flag attr_once;
   static cudaError_t attr_rc = cudaSuccess;
   std::call_once(attr_once, [] {
-    attr_rc = cudaFuncSetAttribute(k_gemm16<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_rc = cudaFuncSetAttribute(k_gemm16<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (attr_rc == cudaSuccess)
-      attr_rc = cudaFuncSetAttribute(k_gemm16<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      attr_rc = cudaFuncSetAttribute(k_gemm16<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (attr_rc == cudaSuccess)
+      attr_rc = cudaFuncSetAttribute(k_gemm16<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (attr_rc == cudaSuccess)
+      attr_rc = cudaFuncSetAttribute(k_gemm16<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   if (attr_rc != cudaSuccess) return MB_ERR_CUDA;
-  const int mt = (int)(M / BM), nt = (int)(N / BN);
+  const int mt = (int)(M / (pair ? 2 * BM : BM)), nt = (int)(N / BN);
   int tiles = mt * nt;
   if (q.sym) {
     tiles = 0;
-    for (int bn = 0; bn < nt; ++bn) tiles += mt < 2 * bn + 2 ? mt : 2 * bn + 2;
+    for (int bn = 0; bn < nt; ++bn) {
+      const int h = pair ? bn + 1 : 2 * bn + 2;  // tiles of column bn not entirely below the diagonal
+      tiles += mt < h ? mt : h;
+    }
   }
   if ((int64_t)tiles * q.batch > (int64_t)1 << 30) return MB_ERR_ARG;
   Args g{};
@@ -676,9 +871,47 @@ int gemm16(const GemmCall& q, cudaStream_t stream) {
     if (sms <= 0) sms = 148;
   }
   const int64_t work = (int64_t)tiles * q.batch;
+  if (pair) {
+    static int pairs = 0;  // co-resident CTA pairs (clusters of 2 live within one GPC)
+    if (pairs == 0) {
+      cudaLaunchConfig_t occ = {};
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 2;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      occ.gridDim = dim3(2 * (sms / 2), 1, 1);
+      occ.blockDim = dim3(kGemmThreads, 1, 1);
+      occ.dynamicSmemBytes = SMEM_BYTES;
+      occ.attrs = at;
+      occ.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, f16 ? k_gemm16<true, true> : k_gemm16<false, true>, &occ) !=
+              cudaSuccess ||
+          n <= 0)
+        return MB_ERR_CUDA;
+      pairs = n;
+    }
+    const int units = (int)(work < pairs ? work : pairs);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * units, 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = stream;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    const cudaError_t rc = f16 ? cudaLaunchKernelEx(&cfg, k_gemm16<true, true>, ma, mbm, g)
+                               : cudaLaunchKernelEx(&cfg, k_gemm16<false, true>, ma, mbm, g);
+    return rc == cudaSuccess && cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA;
+  }
   const int grid = (int)(work < sms ? work : sms);
-  if (f16) k_gemm16<true><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
-  else k_gemm16<false><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
+  if (f16) k_gemm16<true, false><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
+  else k_gemm16<false, false><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
   return cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA;
 }
 
