@@ -647,8 +647,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             umma_commit(&empty[s]);
           }
         }
-        if constexpr (kPair) umma_commit_both(&acc_full[a]);
-        else umma_commit(&acc_full[a]);
+        if constexpr (kPair) {
+          // an aborted tile is not handed over: the odd CTA cannot see this CTA's
+          // abort flag, so its epilogue must time out rather than store the tile
+          if (!*abort_flag) umma_commit_both(&acc_full[a]);
+        } else {
+          umma_commit(&acc_full[a]);
+        }
       }
       if (*abort_flag) {
         // every MMA this thread issued completes (bounded) before the accumulators are freed
