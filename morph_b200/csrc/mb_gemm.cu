@@ -22,7 +22,8 @@
 // While the epilogue drains tile i from one accumulator, the MMAs of tile
 // i + 1 fill the other.
 //
-// Pair mode (MB_GEMM_PAIR=1 in the environment, M % 256 == 0): clusters of two
+// Pair mode (the default when M % 256 == 0; MB_GEMM_PAIR=0 in the environment
+// turns it off): clusters of two
 // CTAs on two SMs share one 256 x 256 output tile through tcgen05.mma
 // .cta_group::2 (M = 256). Each CTA loads its own 128 rows of A and 128 of the
 // 256 rows of B (no multicast), so an SM moves 32 KiB per 64-deep k-block
@@ -776,14 +777,39 @@ bool make_map(CUtensorMap* map, const void* base, int64_t batch, int64_t rows, i
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Pair mode is opt-in while it is measured: MB_GEMM_PAIR=1 in the environment
-// (read once per process).
+// Pair mode unless MB_GEMM_PAIR=0 in the environment (read once per process).
 bool pair_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("MB_GEMM_PAIR");
-    return e != nullptr && e[0] == '1';
+    return e == nullptr || e[0] != '0';
   }();
   return on;
+}
+
+// Co-resident CTA pairs of the pair kernel on this device (clusters of two live
+// within one GPC), or 0 when none can be placed: the single-CTA kernel runs then.
+int pair_units(bool f16, int sms) {
+  static int units[2] = {-1, -1};
+  int& n = units[f16 ? 1 : 0];
+  if (n < 0) {
+    cudaLaunchConfig_t occ = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    occ.gridDim = dim3(2 * (sms / 2), 1, 1);
+    occ.blockDim = dim3(kGemmThreads, 1, 1);
+    occ.dynamicSmemBytes = SMEM_BYTES;
+    occ.attrs = at;
+    occ.numAttrs = 1;
+    int c = 0;
+    const cudaError_t rc =
+        cudaOccupancyMaxActiveClusters(&c, f16 ? k_gemm16<true, true> : k_gemm16<false, true>, &occ);
+    if (rc != cudaSuccess) cudaGetLastError();  // clear it: the single-CTA kernel takes over
+    n = rc == cudaSuccess && c > 0 ? c : 0;
+  }
+  return n;
 }
 
 }  // namespace gemm
@@ -816,12 +842,6 @@ int gemm16(const GemmCall& q, cudaStream_t stream) {
   // symmetric mode writes the lower triangle through dt == d (square output, no other outputs)
   if (q.sym && (M != N || !q.d || q.dt != q.d || q.lddt != q.ldd || q.sdt != q.sd || q.df || q.upd_w))
     return MB_ERR_ARG;
-  // pair mode (opt-in): 256-row tiles over CTA pairs
-  const bool pair = pair_enabled() && M % (2 * BM) == 0;
-  CUtensorMap ma, mbm;
-  if (!make_map(&ma, q.a, q.batch, M, K, q.lda, q.sa, BM, f16) ||
-      !make_map(&mbm, q.b, q.batch, N, K, q.ldb, q.sb, pair ? BM : BN, f16))
-    return MB_ERR_CUDA;
   static std::once_flag attr_once;
   static cudaError_t attr_rc = cudaSuccess;
   std::call_once(attr_once, [] {
@@ -834,6 +854,20 @@ int gemm16(const GemmCall& q, cudaStream_t stream) {
       attr_rc = cudaFuncSetAttribute(k_gemm16<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   if (attr_rc != cudaSuccess) return MB_ERR_CUDA;
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  // pair mode: 256-row tiles over CTA pairs
+  const int pairs = pair_enabled() && M % (2 * BM) == 0 ? pair_units(f16, sms) : 0;
+  const bool pair = pairs > 0;
+  CUtensorMap ma, mbm;
+  if (!make_map(&ma, q.a, q.batch, M, K, q.lda, q.sa, BM, f16) ||
+      !make_map(&mbm, q.b, q.batch, N, K, q.ldb, q.sb, pair ? BM : BN, f16))
+    return MB_ERR_CUDA;
   const int mt = (int)(M / (pair ? 2 * BM : BM)), nt = (int)(N / BN);
   int tiles = mt * nt;
   if (q.sym) {
@@ -868,35 +902,8 @@ int gemm16(const GemmCall& q, cudaStream_t stream) {
   g.upd_stage_out = q.upd_out != nullptr && q.upd_cols % 8 == 0;
   for (int b = 0; b < q.batch && g.upd_stage_out; ++b) g.upd_stage_out = aligned(q.upd_out[b], 16);
   take_fault(kFaultGemm, &g.fault.unit, &g.fault.limit_ns);
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
   const int64_t work = (int64_t)tiles * q.batch;
   if (pair) {
-    static int pairs = 0;  // co-resident CTA pairs (clusters of 2 live within one GPC)
-    if (pairs == 0) {
-      cudaLaunchConfig_t occ = {};
-      cudaLaunchAttribute at[1];
-      at[0].id = cudaLaunchAttributeClusterDimension;
-      at[0].val.clusterDim.x = 2;
-      at[0].val.clusterDim.y = 1;
-      at[0].val.clusterDim.z = 1;
-      occ.gridDim = dim3(2 * (sms / 2), 1, 1);
-      occ.blockDim = dim3(kGemmThreads, 1, 1);
-      occ.dynamicSmemBytes = SMEM_BYTES;
-      occ.attrs = at;
-      occ.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, f16 ? k_gemm16<true, true> : k_gemm16<false, true>, &occ) !=
-              cudaSuccess ||
-          n <= 0)
-        return MB_ERR_CUDA;
-      pairs = n;
-    }
     const int units = (int)(work < pairs ? work : pairs);
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
