@@ -270,8 +270,11 @@ MB_API int mb_sparse_rows_update(float* w, float* m, float* v, int64_t rows, int
  * [m, n] with pitches ldc/ldd; dt (optional) receives out^T as [n, m] with
  * pitch lddt; df (optional) receives out in FP32 with pitch lddf. m must be a
  * multiple of 128, n of 256 and k of 64 (pad with zeros). A wait that exceeds
- * its bound sets *err_flag (device int32) to 1. These are the matmuls of
- * orthogonalize, streamtrain/optimizer.py:20-21. */
+ * its bound sets *err_flag (device int32) to 1. When m is a multiple of 256 the
+ * launch runs as clusters of two CTAs (tcgen05 cta_group::2, M = 256 over two
+ * SMs) unless MB_GEMM_PAIR=0 is set in the environment; the results are the
+ * same bits either way. These are the matmuls of orthogonalize,
+ * streamtrain/optimizer.py:20-21. */
 MB_API int mb_gemm16(int32_t dtype, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
                      int64_t k, float alpha, float beta, const void* c, int64_t ldc, void* d, int64_t ldd, void* dt,
                      int64_t lddt, float* df, int64_t lddf, int32_t* err_flag, mb_stream_t stream);
