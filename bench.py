@@ -149,18 +149,53 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
+REF_DIR = os.path.join(REPO, "baseline", "_ref")
+
+
+def installed_reference_optimizer():
+    """The reference's streamtrain.optimizer as installed (unmodified) in
+    baseline/_ref by __graft_entry__.install_reference(), or None."""
+    if not os.path.isdir(os.path.join(REF_DIR, "streamtrain")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.append(REF_DIR)
+    try:
+        import streamtrain.optimizer as ref_opt
+    except Exception:
+        return None
+    return ref_opt
+
+
 def reference_muon_cpu_time(shape, seed=0):
-    """Seconds of one Muon matrix step of the reference on the host cores:
-    streamtrain/optimizer.py:52-61 with orthogonalize (optimizer.py:13-22) in
-    FP32 torch on the CPU, restated here (the reference tree is not read at run
-    time). One warm-up, one timed step."""
+    """Seconds of one Muon matrix step of the reference on the host cores, and
+    how it was run: the installed reference's HybridMuonAdamW.step
+    (streamtrain/optimizer.py:48-62) on a one-matrix model when baseline/_ref
+    holds it ("reference"), else the same arithmetic restated here ("port").
+    One warm-up, one timed step."""
     threads = cpu_threads()
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(seed)
+    lr, wd = 3e-4, .1
+    ref = installed_reference_optimizer()
+    if ref is not None:
+        # the Linear weight is [rows, cols] = shape; the LayerNorm gives the AdamW group a parameter
+        model = torch.nn.Sequential(torch.nn.Linear(shape[1], shape[0], bias=False), torch.nn.LayerNorm(8))
+        grad = (torch.randn(shape, generator=g) * 1e-4).bfloat16().float()
+        opt = ref.HybridMuonAdamW(model, lr=lr, weight_decay=wd)
+
+        def ref_step():
+            model[0].weight.grad = grad
+            for q in model[1].parameters():
+                q.grad = torch.zeros_like(q)
+            opt.step()
+
+        ref_step()
+        t0 = time.perf_counter()
+        ref_step()
+        return time.perf_counter() - t0, threads, "reference"
     p = torch.randn(shape, generator=g) * .02
     mom = torch.zeros(shape)
     grad = (torch.randn(shape, generator=g) * 1e-4).bfloat16()
-    lr, wd = 3e-4, .1
 
     def step():
         gf = grad.float()
@@ -181,7 +216,7 @@ def reference_muon_cpu_time(shape, seed=0):
     step()
     t0 = time.perf_counter()
     step()
-    return time.perf_counter() - t0, threads
+    return time.perf_counter() - t0, threads, "port"
 
 
 def reference_cpu_step_time(layers=1, steps=3, warmup=1, seed=0):
@@ -613,15 +648,17 @@ def run_config4(args, emit=True):
         counts = {}
         for q in opt.muon:
             counts[tuple(q.shape)] = counts.get(tuple(q.shape), 0) + 1
-        est, threads, sample = 0.0, 1, {}
+        est, threads, sample, kind = 0.0, 1, {}, "port"
         for shape, cnt in counts.items():
-            sec, threads = reference_muon_cpu_time(shape)
+            sec, threads, kind = reference_muon_cpu_time(shape)
             sample[f"{shape[0]}x{shape[1]}"] = sec
             est += sec * cnt
-        line["cpu_baseline"] = {"value": est, "unit": "s/step", "cores": threads, "kind": "reference",
-                                "sample": "one Muon step (optimizer.py:52-61, FP32 orthogonalize) of each matrix "
-                                          "shape on the host cores, scaled by the shape counts; the AdamW group "
-                                          "(4% of the parameters, <1% of the work) is not included",
+        how = ("the installed reference's HybridMuonAdamW.step on a one-matrix model" if kind == "reference"
+               else "optimizer.py:52-61 with FP32 orthogonalize, restated")
+        line["cpu_baseline"] = {"value": est, "unit": "s/step", "cores": threads, "kind": kind,
+                                "sample": f"one Muon step ({how}) of each matrix shape on the host cores, scaled "
+                                          "by the shape counts; the AdamW group (4% of the parameters, <1% of the "
+                                          "work) is not included",
                                 "per_matrix_s": sample}
     if emit:
         print(json.dumps(line), flush=True)
