@@ -1056,7 +1056,8 @@ def run_config5(args, rank=0, world=1, local_rank=0, emit=True):
         ref_times, threads = reference_rows_cpu_time(k, cols)
         line["cpu_baseline"] = {"value": k * cols / (sum(ref_times) / len(ref_times)), "unit": "touched params/s",
                                 "cores": threads, "kind": "reference",
-                                "sample": "disk.py:210-215 arithmetic on the gathered [26214, 3072] rows in RAM"}
+                                "sample": "the torch calls of streamtrain/disk.py:210-215 (DiskState.update "
+                                          "without its memmap and fsync) on the gathered [26214, 3072] rows in RAM"}
     if emit:
         print(json.dumps(line), flush=True)
     return line
