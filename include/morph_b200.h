@@ -295,6 +295,8 @@ typedef struct mb_muon_args {
   const int32_t* skip; /* optional device flag (e.g. &mb_step_state.skip of a gate
                           finalized earlier on the stream): nonzero = every launch
                           of the step returns at once and nothing changes */
+  int32_t max_sms;     /* 0: the GEMMs use every SM; else at most this many, leaving
+                          the rest to work on other streams (e.g. a collective) */
 } mb_muon_args;
 
 /* Most matrices one mb_muon_step_batched call takes. */

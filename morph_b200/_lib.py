@@ -72,7 +72,7 @@ class Plan(ctypes.Structure):
 class MuonArgs(ctypes.Structure):
     _fields_ = [("beta_lerp", _f), ("nesterov", _f), ("ns_a", _f), ("ns_b", _f), ("ns_c", _f),
                 ("ns_steps", _i32), ("shape_scale", _f), ("cwd", _f), ("neg_lr", _f), ("ns_dtype", _i32),
-                ("skip", _p)]
+                ("skip", _p), ("max_sms", _i32)]
 
 
 class HostScalars(ctypes.Structure):

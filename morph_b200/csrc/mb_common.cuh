@@ -238,6 +238,7 @@ struct GemmCall {
   float upd_scale, upd_cwd, upd_neglr;
   int32_t* err;
   const int32_t* skip;  // optional device flag: nonzero = the launch returns at once
+  int max_sms = 0;      // 0: persistent grid over every SM; else at most this many SMs
 };
 int gemm16(const GemmCall& call, cudaStream_t stream);
 

@@ -904,7 +904,8 @@ int gemm16(const GemmCall& q, cudaStream_t stream) {
   take_fault(kFaultGemm, &g.fault.unit, &g.fault.limit_ns);
   const int64_t work = (int64_t)tiles * q.batch;
   if (pair) {
-    const int units = (int)(work < pairs ? work : pairs);
+    int units = (int)(work < pairs ? work : pairs);
+    if (q.max_sms > 0 && units > q.max_sms / 2) units = q.max_sms / 2 > 0 ? q.max_sms / 2 : 1;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
@@ -921,7 +922,8 @@ int gemm16(const GemmCall& q, cudaStream_t stream) {
                                : cudaLaunchKernelEx(&cfg, k_gemm16<false, true>, ma, mbm, g);
     return rc == cudaSuccess && cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA;
   }
-  const int grid = (int)(work < sms ? work : sms);
+  int grid = (int)(work < sms ? work : sms);
+  if (q.max_sms > 0 && grid > q.max_sms) grid = q.max_sms;
   if (f16) k_gemm16<true, false><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
   else k_gemm16<false, false><<<grid, kGemmThreads, SMEM_BYTES, stream>>>(ma, mbm, g);
   return cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA;

@@ -78,6 +78,7 @@ struct MuonParams {
   float beta_lerp;  // .05
   float nesterov;   // .95
   const int32_t* skip = nullptr;  // device flag: nonzero = the step changes nothing
+  int max_sms = 0;                // the GEMMs' SM cap (0: every SM)
 };
 
 // Nesterov input of one element (also writes the updated momentum when `write`).
@@ -372,6 +373,7 @@ int ns_core(const MuonSrc& t, const MuonParams& p, int gdt, int batch, int64_t r
     g1.dt = A; g1.lddt = mp; g1.sdt = sa;
     g1.err = err;
     g1.skip = p.skip;
+    g1.max_sms = p.max_sms;
     if ((rc = gemm16(g1, s))) return rc;
     // M = a I + b A + c A A, formed in FP32 and rounded once: the reference's
     // a X + (b A + c A A) X would add two nearly cancelling products.
@@ -386,6 +388,7 @@ int ns_core(const MuonSrc& t, const MuonParams& p, int gdt, int batch, int64_t r
     g2.dt = B; g2.lddt = mp; g2.sdt = sa;
     g2.err = err;
     g2.skip = p.skip;
+    g2.max_sms = p.max_sms;
     if ((rc = gemm16(g2, s))) return rc;
     // X' = M X: X^T is the K-major operand. X' overwrites X (no longer read);
     // X'^T goes to the other XT buffer. The last iteration applies the update
@@ -398,6 +401,7 @@ int ns_core(const MuonSrc& t, const MuonParams& p, int gdt, int batch, int64_t r
     g3.alpha = s1;
     g3.err = err;
     g3.skip = p.skip;
+    g3.max_sms = p.max_sms;
     if (!last) {
       g3.d = X; g3.ldd = np; g3.sd = sx;
       g3.dt = XTn; g3.lddt = mp; g3.sdt = sx;
@@ -481,7 +485,8 @@ MB_API int mb_muon_step_batched(float* const* w, float* const* momentum, const v
   Layout L = layout_for(batch, rows, cols, false);
   if (workspace_bytes < L.total) return MB_ERR_ARG;
   if (!aligned(workspace, 256)) return MB_ERR_ALIGN;
-  MuonParams p{args->beta_lerp, args->nesterov, args->skip};
+  if (args->max_sms < 0) return MB_ERR_ARG;
+  MuonParams p{args->beta_lerp, args->nesterov, args->skip, args->max_sms};
   const float coeffs[3] = {args->ns_a, args->ns_b, args->ns_c};
   Update upd{w, out_dtype == MB_NONE ? nullptr : out, out_dtype, args->shape_scale, args->cwd, args->neg_lr};
   return ns_core(t, p, grad_dtype, batch, rows, cols, args->ns_steps, coeffs, args->ns_dtype, &upd,

@@ -136,14 +136,17 @@ def batch_plan(count, rows, cols, workspace_limit):
     return [min(size, count - b) for b in range(0, count, size)]
 
 
-def muon_step_batched(params, moms, grads, outs, lr, weight_decay, ns_dtype="auto", err=None, skip=None):
+def muon_step_batched(params, moms, grads, outs, lr, weight_decay, ns_dtype="auto", err=None, skip=None,
+                      max_sms=0):
     """optimizer.py:52-61 for each of ``params`` (same-shape contiguous FP32 CUDA
     matrices on one device) in one kernel-4 call: momentum (FP32, in place),
     Nesterov blend, Newton-Schulz, shape scale, decoupled weight decay; ``outs``
     (optional, one 16-bit tensor each) receive the updated weights. ``err``
     (int32 device flag) is raised when a bounded wait expires. ``skip`` (device
     address of an int32 flag, e.g. a finalized gate's skip) makes every launch
-    of the step return at once when the flag is set: nothing changes."""
+    of the step return at once when the flag is set: nothing changes.
+    ``max_sms`` (0: all) caps the SMs the GEMMs occupy, leaving the rest to
+    kernels on other streams (a collective); the results are the same bits."""
     batch = len(params)
     if batch == 0:
         return
@@ -170,7 +173,7 @@ def muon_step_batched(params, moms, grads, outs, lr, weight_decay, ns_dtype="aut
     f = lambda x: float(np.float32(x))  # noqa: E731
     args = _lib.MuonArgs(f(.05), f(.95), f(NS_COEFFS[0]), f(NS_COEFFS[1]), f(NS_COEFFS[2]), 5,
                          f(max(1, rows / cols) ** .5), f(1 - lr * weight_decay), f(-lr),
-                         ns_operand_dtype(rows, cols, ns_dtype), skip)
+                         ns_operand_dtype(rows, cols, ns_dtype), skip, int(max_sms))
     odt = _lib.MB_NONE if outs is None else _lib.dtype_code(outs[0].dtype)
     table = ctypes.c_void_p * batch
     with torch.cuda.device(dev):

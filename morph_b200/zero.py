@@ -449,10 +449,11 @@ def deal_matrices(shapes, world, rank_batches):
 class CudaHybridBackend:
     """Kernel calls of one sharded Hybrid step on the rank's GPU (C-ABI library)."""
 
-    def __init__(self, device, ns_dtype="auto"):
+    def __init__(self, device, ns_dtype="auto", max_sms=0):
         self.device = torch.device(device)
         self.engine = StepEngine(self.device)
         self.ns_dtype = ns_dtype
+        self.max_sms = int(max_sms)  # the Muon GEMMs' SM cap (0: all): the rest run the all-gathers
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._keys = {}
         self._plan = None
@@ -497,7 +498,7 @@ class CudaHybridBackend:
     def muon_batch(self, params, moms, grads, outs, lr, weight_decay, skip=None):
         """One kernel-4 step over a batch; ``skip``: device address of a skip flag."""
         from .muon import muon_step_batched
-        muon_step_batched(params, moms, grads, outs, lr, weight_decay, self.ns_dtype, self.err, skip)
+        muon_step_batched(params, moms, grads, outs, lr, weight_decay, self.ns_dtype, self.err, skip, self.max_sms)
 
     def check_errors(self):
         """Raise RuntimeError if a bounded wait of a Muon launch expired (waits for the stream)."""
@@ -527,6 +528,10 @@ class ZeroHybridMuonAdamW:
       3. the AdamW group's ZeRO-1 step, finalized from the same record (no
          second statistics pass or all-reduce; kernel 1 and its all-gathers).
 
+    With several ranks the Muon GEMMs occupy at most (SMs - ``reserve_sms``)
+    SMs, so NCCL's all-gather of one round runs beside the next round's GEMMs
+    (a persistent GEMM grid over every SM would hold it off until a launch ends).
+
     A refused step changes nothing on any rank (the all-gathers carry the
     unchanged weights). With ``sync=True`` (the default, the reference's
     behaviour) ``step`` then raises FloatingPointError on every rank; with
@@ -537,7 +542,7 @@ class ZeroHybridMuonAdamW:
 
     def __init__(self, model=None, lr=1e-3, muon_lr=None, weight_decay=.01, *, params=None, muon=None,
                  low_precision=torch.bfloat16, process_group=None, device=None, backend=None, adam_backend=None,
-                 ns_dtype="auto", workspace_limit=4 << 30, adam_rounds=4, sync=True):
+                 ns_dtype="auto", workspace_limit=4 << 30, adam_rounds=4, sync=True, reserve_sms=8):
         from .muon import batch_plan, partition
         if model is not None:
             muon_list, adam_list = partition(model)
@@ -563,10 +568,15 @@ class ZeroHybridMuonAdamW:
         for p in self.muon:
             if p.dim() != 2:
                 raise ValueError("Muon parameters must be 2-D")
-        self.backend = backend if backend is not None else CudaHybridBackend(self.device, ns_dtype)
         if backend is None:
+            # with several ranks the Muon GEMMs leave reserve_sms SMs to NCCL's round all-gathers,
+            # which could otherwise start only between GEMM launches (the GEMM grid fills every SM)
+            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+            cap = max(2, sms - int(reserve_sms)) if self.world > 1 and reserve_sms else 0
+            self.backend = CudaHybridBackend(self.device, ns_dtype, cap)
             plan = lambda n, r, c: batch_plan(n, r, c, workspace_limit)  # noqa: E731
         else:
+            self.backend = backend
             plan = getattr(backend, "batch_plan", lambda n, r, c: [n] if n else [])
         self.rounds = deal_matrices([tuple(p.shape) for p in self.muon], self.world, plan)
         # flat low-precision buffer of the Muon group: per round, one equal block per rank

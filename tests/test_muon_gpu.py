@@ -219,6 +219,28 @@ def test_batched_step_bit_identical_to_one_matrix_calls(cuda, shape, gdt):
         assert _rel(w2[b].cpu().numpy() - decay, w_ref - decay) < 1e-2
 
 
+@pytest.mark.parametrize("max_sms", [20, 7, 1])
+def test_sm_cap_changes_no_bit(cuda, max_sms):
+    """mb_muon_args.max_sms caps the GEMMs' grid (pair-CTA and single-CTA
+    launches alike); the step's results are the same bits as with every SM."""
+    from morph_b200.muon import muon_step_batched
+    shape = (512, 1280)  # padded M = 512: pair-CTA tiles
+    gen = torch.Generator(device=cuda).manual_seed(17)
+    w0 = [torch.randn(shape, device=cuda, generator=gen) * .02 for _ in range(3)]
+    gs = [(torch.randn(shape, device=cuda, generator=gen) * 1e-3).bfloat16() for _ in range(3)]
+    out = []
+    for cap in (0, max_sms):
+        ws = [w.clone() for w in w0]
+        ms = [torch.zeros_like(w) for w in w0]
+        os_ = [torch.empty(shape, dtype=torch.bfloat16, device=cuda) for _ in w0]
+        for _ in range(2):
+            muon_step_batched(ws, ms, gs, os_, .02, .01, "bf16", max_sms=cap)
+        out.append(ws + ms + os_)
+    torch.cuda.synchronize()
+    for a, b in zip(*out):
+        assert torch.equal(a, b)
+
+
 def test_batched_step_rejects_bad_arguments(cuda):
     import ctypes
     from morph_b200 import _lib
