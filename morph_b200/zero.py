@@ -528,9 +528,9 @@ class ZeroHybridMuonAdamW:
       3. the AdamW group's ZeRO-1 step, finalized from the same record (no
          second statistics pass or all-reduce; kernel 1 and its all-gathers).
 
-    With several ranks the Muon GEMMs occupy at most (SMs - ``reserve_sms``)
-    SMs, so NCCL's all-gather of one round runs beside the next round's GEMMs
-    (a persistent GEMM grid over every SM would hold it off until a launch ends).
+    ``reserve_sms`` (with several ranks) caps the Muon GEMMs at SMs -
+    reserve_sms, leaving SMs to NCCL's round all-gathers; 0 (the default, the
+    faster setting measured at N=2) gives the GEMMs every SM.
 
     A refused step changes nothing on any rank (the all-gathers carry the
     unchanged weights). With ``sync=True`` (the default, the reference's
@@ -542,7 +542,7 @@ class ZeroHybridMuonAdamW:
 
     def __init__(self, model=None, lr=1e-3, muon_lr=None, weight_decay=.01, *, params=None, muon=None,
                  low_precision=torch.bfloat16, process_group=None, device=None, backend=None, adam_backend=None,
-                 ns_dtype="auto", workspace_limit=4 << 30, adam_rounds=4, sync=True, reserve_sms=8):
+                 ns_dtype="auto", workspace_limit=4 << 30, adam_rounds=4, sync=True, reserve_sms=0):
         from .muon import batch_plan, partition
         if model is not None:
             muon_list, adam_list = partition(model)
@@ -569,8 +569,7 @@ class ZeroHybridMuonAdamW:
             if p.dim() != 2:
                 raise ValueError("Muon parameters must be 2-D")
         if backend is None:
-            # with several ranks the Muon GEMMs leave reserve_sms SMs to NCCL's round all-gathers,
-            # which could otherwise start only between GEMM launches (the GEMM grid fills every SM)
+            # with several ranks the Muon GEMMs may leave reserve_sms SMs to NCCL's round all-gathers
             sms = torch.cuda.get_device_properties(self.device).multi_processor_count
             cap = max(2, sms - int(reserve_sms)) if self.world > 1 and reserve_sms else 0
             self.backend = CudaHybridBackend(self.device, ns_dtype, cap)
