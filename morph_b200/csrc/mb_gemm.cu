@@ -23,14 +23,17 @@
 // i + 1 fill the other.
 //
 // Pair mode (the default when M % 256 == 0; MB_GEMM_PAIR=0 in the environment
-// turns it off): clusters of two
-// CTAs on two SMs share one 256 x 256 output tile through tcgen05.mma
-// .cta_group::2 (M = 256). Each CTA loads its own 128 rows of A and 128 of the
-// 256 rows of B (no multicast), so an SM moves 32 KiB per 64-deep k-block
-// instead of 48 KiB; the even CTA issues the MMAs and its commits arrive on
-// both CTAs' barriers; each CTA's TMEM holds its 128 rows of the accumulator
-// and its own epilogue drains them. The odd CTA's loads and epilogue signal the
-// even CTA's barriers through their cluster addresses.
+// turns it off): clusters of two CTAs on two SMs share one 256 x 256 output
+// tile through tcgen05.mma .cta_group::2 (M = 256). Each CTA loads its own 128
+// rows of A and 128 of the 256 rows of B (no multicast) into a 6-stage ring, so
+// an SM moves 32 KiB per 64-deep k-block instead of 48 KiB; the even CTA issues
+// the MMAs and its commits arrive on both CTAs' barriers; each CTA's TMEM holds
+// its 128 rows of the accumulator and its own epilogue drains them. The odd
+// CTA's loads and epilogue signal the even CTA's barriers through their cluster
+// addresses. The cluster barrier (not bounded) runs only at start-up and
+// before TMEM is freed, after every bounded wait of both CTAs has ended.
+// GemmCall.max_sms (0: all) caps the persistent grid, leaving SMs to kernels on
+// other streams.
 //
 // Symmetric mode (the output is known symmetric, e.g. X X^T and polynomials
 // of it): only tiles not entirely below the diagonal are computed; elements on
