@@ -3,6 +3,7 @@
  * checks of device entry points (which fail before touching a GPU). Exits 0 on
  * success; prints the failing check otherwise. */
 #include <stdio.h>
+#include <stddef.h>
 #include <string.h>
 
 #include "morph_b200.h"
@@ -19,6 +20,7 @@ int main(void) {
   CHECK(mb_version() >= 1);
   CHECK(strncmp(mb_status_string(MB_ERR_NONFINITE), "nonfinite gradient", 18) == 0);
   CHECK(sizeof(mb_segment) == 64 && sizeof(mb_group) == 32 && sizeof(mb_step_state) == 96);
+  CHECK(sizeof(mb_muon_args) == 56 && offsetof(mb_muon_args, max_sms) == 48);
 
   mb_step_state st;
   CHECK(mb_step_state_init(&st, 65536.0, 2000) == MB_OK);

@@ -93,3 +93,20 @@ def test_fault_arming_is_host_only_and_validated():
     for kernel in (_lib.MB_FAULT_APPLY, _lib.MB_FAULT_STATS, _lib.MB_FAULT_GEMM):
         assert L.mb_debug_arm_fault(kernel, 7, 5_000_000) == _lib.MB_OK
     assert L.mb_debug_arm_fault(0, -1, 0) == _lib.MB_OK
+
+
+def test_muon_args_layout_and_sm_cap_validation():
+    """mb_muon_args as Python binds it (skip pointer, then the SM cap), and a
+    negative max_sms is refused before anything reaches a device (the pointers
+    here are never dereferenced)."""
+    assert ctypes.sizeof(_lib.MuonArgs) == 56
+    assert _lib.MuonArgs.skip.offset == 40 and _lib.MuonArgs.max_sms.offset == 48
+    L = _lib.lib()
+    rows, cols = 256, 512
+    nbytes = L.mb_muon_batch_workspace_bytes(1, rows, cols)
+    assert nbytes > 0
+    fake = (ctypes.c_void_p * 1)(4096)
+    args = _lib.MuonArgs(.05, .95, 3.4445, -4.775, 2.0315, 5, 1.0, 1.0, -1e-3, _lib.MB_BF16, None, -1)
+    rc = L.mb_muon_step_batched(fake, fake, fake, _lib.MB_BF16, None, _lib.MB_NONE, 1, rows, cols,
+                                ctypes.byref(args), 4096, nbytes, None, None)
+    assert rc == _lib.MB_ERR_ARG
