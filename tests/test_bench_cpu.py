@@ -27,3 +27,14 @@ def test_reference_arm_prints_the_contract_line():
     e2e = line["e2e"]
     assert e2e["value"] == line["value"] and e2e["unit"] == line["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_config4_cpu_baseline_runs_the_installed_reference():
+    """Config 4's cpu_baseline times the reference's own HybridMuonAdamW.step
+    (from baseline/_ref) when it is installed, else the restated arithmetic."""
+    sys.path.insert(0, REPO)
+    import bench
+    sec, threads, kind = bench.reference_muon_cpu_time((256, 384))
+    assert sec > 0 and threads >= 1
+    installed = os.path.isdir(os.path.join(REPO, "baseline", "_ref", "streamtrain"))
+    assert kind == ("reference" if installed else "port")
