@@ -1492,7 +1492,7 @@ def _summary(line):
     """The fields of a config's own line kept in the headline line's ``configs``."""
     keep = ("metric", "value", "unit", "ms_per_step", "higher_is_better", "n_gpus", "steps", "warmup", "dtype",
             "roofline", "clocks", "cpu_baseline", "eager_us_per_step", "eager_device_us_per_step",
-            "graph_replay_us_per_step", "per_matrix")
+            "graph_replay_us_per_step", "graph_replay_trials_us", "graph_replay_device_us_per_step", "per_matrix")
     out = {k: line[k] for k in keep if k in line}
     out["workload"] = line.get("config", {}).get("workload")
     out["parallelism"] = line.get("config", {}).get("parallelism")
